@@ -1,0 +1,406 @@
+/*
+ * zlift_oracle.c -- TEST INFRASTRUCTURE, NOT PRODUCT CODE.
+ *
+ * A plain-C restatement of the reference's CPU arithmetic for the GEMM and
+ * fused-attention hot path.  It is the checker for the CUDA kernels in
+ * zlift_b200/csrc: only tests/, __graft_entry__.smoke() and bench.py's CPU
+ * baseline leg may load it.  The product library never links or calls it.
+ *
+ * What each function restates (paths relative to the zLift project root):
+ *   zo_half_to_float / zo_float_to_half  zblas/zblas.c:241-277
+ *       (fp16 RNE for normals, TRUNCATION for subnormals, overflow -> inf)
+ *   zo_bf16_to_float / zo_float_to_bf16  zblas/zblas.c:306-317
+ *       (bf16 RNE with no NaN special case)
+ *   zo_sgemm                              cblas_sgemm as called at
+ *       zblas/zblas.c:127 (column-major, op in {N,T,C}); products are summed
+ *       in double and rounded once, which is at least as accurate as the
+ *       single-precision BLAS the reference links.
+ *   zo_gemm_ex                            cublasGemmEx, zblas/zblas.c:357-391,
+ *       with gemm_ex_host (zblas/zblas.c:318-356): widen A/B (and a narrow C)
+ *       to fp32, run the fp32 GEMM, narrow C with the reference converter.
+ *       The int8 x int8 -> int32 branch (Atype=Btype=CUDA_R_8I, Ctype=
+ *       CUDA_R_32I, compute 32I) has no counterpart in the reference (which
+ *       returns NOT_SUPPORTED, zblas/zblas.c:366-367); it is exact int32
+ *       arithmetic with two's-complement wrap for alpha/beta scaling.
+ *   zo_gemm_strided_batched_ex            zblas/zblas.c:491-511 (host loop
+ *       over the batch; strides in elements, elem_size :488-490).
+ *   zo_attention / zo_attention_rows      the fp32 math of fmha_f32
+ *       (zblas/zblas_gpu.cpp:793-844) with the masking and rounding points
+ *       of fmha_run (zblas/zblas_gpu.cpp:892-1039): causal mask
+ *       `key > query + diag` (:967), fully-masked rows give O = 0 (:981,
+ *       :991, :1015), P rounded to the input type before P.V (:1001, via
+ *       joint_matrix_copy), O accumulated wide and rounded once (:1013-1023).
+ *       The log-sum-exp output (natural log, m + log(l)) is not produced by
+ *       the reference at all; it follows the flash-attention convention.
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+enum { ZO_OP_N = 0, ZO_OP_T = 1, ZO_OP_C = 2 };
+enum { ZO_R_32F = 0, ZO_R_16F = 2, ZO_R_8I = 3, ZO_R_32I = 10, ZO_R_16BF = 14 };
+enum { ZO_COMPUTE_32F = 68, ZO_COMPUTE_32I = 72 };
+enum { ZO_OK = 0, ZO_NOT_INITIALIZED = 1, ZO_INVALID_VALUE = 7,
+       ZO_NOT_SUPPORTED = 15 };
+
+/* ---- scalar converters (zblas/zblas.c:241-277, :306-317) -------------- */
+
+float zo_half_to_float(uint16_t h) {
+    uint32_t sign = (h >> 15) & 1u, ex = (h >> 10) & 0x1fu, man = h & 0x3ffu;
+    uint32_t bits;
+    if (ex == 0) {
+        if (man == 0) {
+            bits = sign << 31;
+        } else {                       /* subnormal: renormalise */
+            int shift = 0;
+            while (!(man & 0x400u)) { man <<= 1; shift++; }
+            /* value = 1.m * 2^(-14 - (shift - 1)) ... written via exponent */
+            bits = (sign << 31) | ((uint32_t)(127 - 15 - (shift - 1)) << 23)
+                 | ((man & 0x3ffu) << 13);
+        }
+    } else if (ex == 31) {
+        bits = (sign << 31) | 0x7f800000u | (man << 13);
+    } else {
+        bits = (sign << 31) | ((ex - 15u + 127u) << 23) | (man << 13);
+    }
+    float f;
+    memcpy(&f, &bits, 4);
+    return f;
+}
+
+uint16_t zo_float_to_half(float f) {
+    uint32_t bits;
+    memcpy(&bits, &f, 4);
+    uint32_t sign = (bits >> 16) & 0x8000u;
+    int ex = (int)((bits >> 23) & 0xffu) - 127;
+    uint32_t man = bits & 0x7fffffu;
+    if (ex > 15) return (uint16_t)(sign | 0x7c00u);      /* overflow, inf, NaN */
+    if (ex < -24) return (uint16_t)sign;                 /* underflow to zero */
+    if (ex < -14) {                                      /* subnormal: truncate */
+        man |= 0x800000u;
+        return (uint16_t)(sign | (man >> (13 + (-14 - ex))));
+    }
+    uint32_t h = sign | ((uint32_t)(ex + 15) << 10) | (man >> 13);
+    uint32_t rem = man & 0x1fffu;                        /* round to nearest even */
+    if (rem > 0x1000u || (rem == 0x1000u && (h & 1u))) h++;
+    return (uint16_t)h;
+}
+
+float zo_bf16_to_float(uint16_t b) {
+    uint32_t u = (uint32_t)b << 16;
+    float f;
+    memcpy(&f, &u, 4);
+    return f;
+}
+
+uint16_t zo_float_to_bf16(float f) {
+    uint32_t u;
+    memcpy(&u, &f, 4);
+    u += 0x7fffu + ((u >> 16) & 1u);
+    return (uint16_t)(u >> 16);
+}
+
+/* bulk forms, used by the tests to pin the converters element by element */
+void zo_half_to_float_n(const uint16_t *x, float *y, int64_t n) {
+    for (int64_t i = 0; i < n; i++) y[i] = zo_half_to_float(x[i]);
+}
+void zo_float_to_half_n(const float *x, uint16_t *y, int64_t n) {
+    for (int64_t i = 0; i < n; i++) y[i] = zo_float_to_half(x[i]);
+}
+void zo_bf16_to_float_n(const uint16_t *x, float *y, int64_t n) {
+    for (int64_t i = 0; i < n; i++) y[i] = zo_bf16_to_float(x[i]);
+}
+void zo_float_to_bf16_n(const float *x, uint16_t *y, int64_t n) {
+    for (int64_t i = 0; i < n; i++) y[i] = zo_float_to_bf16(x[i]);
+}
+
+/* ---- column-major operand access ------------------------------------ */
+
+/* element (i, l) of op(X), where X is stored column-major with leading
+ * dimension ld: op N reads X[i + l*ld], op T/C reads X[l + i*ld]. */
+static inline int64_t opidx(int op, int64_t i, int64_t l, int64_t ld) {
+    return op == ZO_OP_N ? i + l * ld : l + i * ld;
+}
+
+static double load_elem(const void *p, int type, int64_t at) {
+    switch (type) {
+    case ZO_R_32F: return ((const float *)p)[at];
+    case ZO_R_16F: return zo_half_to_float(((const uint16_t *)p)[at]);
+    case ZO_R_16BF: return zo_bf16_to_float(((const uint16_t *)p)[at]);
+    case ZO_R_8I: return ((const int8_t *)p)[at];
+    case ZO_R_32I: return ((const int32_t *)p)[at];
+    default: return 0.0;
+    }
+}
+
+/* fp32 GEMM restating cblas_sgemm (zblas/zblas.c:127): C = alpha*op(A)op(B)
+ * + beta*C, column-major.  beta == 0 does not read C (BLAS convention). */
+void zo_sgemm(int transa, int transb, int m, int n, int k, float alpha,
+              const float *A, int lda, const float *B, int ldb, float beta,
+              float *C, int ldc) {
+#pragma omp parallel for schedule(static)
+    for (int j = 0; j < n; j++) {
+        for (int i = 0; i < m; i++) {
+            double acc = 0.0;
+            for (int l = 0; l < k; l++)
+                acc += (double)A[opidx(transa, i, l, lda)]
+                     * (double)B[opidx(transb, l, j, ldb)];
+            double c = (double)alpha * acc;
+            if (beta != 0.0f) c += (double)beta * (double)C[i + (int64_t)j * ldc];
+            C[i + (int64_t)j * ldc] = (float)c;
+        }
+    }
+}
+
+/* int8 x int8 -> int32 with int32 alpha/beta; exact, wrapping. */
+static void gemm_i8(int transa, int transb, int m, int n, int k,
+                    int32_t alpha, const int8_t *A, int lda,
+                    const int8_t *B, int ldb, int32_t beta,
+                    int32_t *C, int ldc) {
+#pragma omp parallel for schedule(static)
+    for (int j = 0; j < n; j++) {
+        for (int i = 0; i < m; i++) {
+            int64_t acc = 0;
+            for (int l = 0; l < k; l++)
+                acc += (int32_t)A[opidx(transa, i, l, lda)]
+                     * (int32_t)B[opidx(transb, l, j, ldb)];
+            uint32_t r = (uint32_t)alpha * (uint32_t)(int32_t)acc;
+            if (beta != 0)
+                r += (uint32_t)beta * (uint32_t)C[i + (int64_t)j * ldc];
+            C[i + (int64_t)j * ldc] = (int32_t)r;
+        }
+    }
+}
+
+/* 16-bit (or fp32) inputs, fp32 compute: restates gemm_ex_host
+ * (zblas/zblas.c:318-356) -- widen, fp32 GEMM, narrow C. */
+static int gemm_wide(int transa, int transb, int m, int n, int k, float alpha,
+                     const void *A, int Atype, int lda, const void *B, int Btype,
+                     int ldb, float beta, void *C, int Ctype, int ldc) {
+#pragma omp parallel for schedule(static)
+    for (int j = 0; j < n; j++) {
+        for (int i = 0; i < m; i++) {
+            double acc = 0.0;
+            for (int l = 0; l < k; l++)
+                acc += load_elem(A, Atype, opidx(transa, i, l, lda))
+                     * load_elem(B, Btype, opidx(transb, l, j, ldb));
+            int64_t at = i + (int64_t)j * ldc;
+            double c = (double)alpha * acc;
+            if (beta != 0.0f) c += (double)beta * load_elem(C, Ctype, at);
+            float cf = (float)c;
+            if (Ctype == ZO_R_16F) ((uint16_t *)C)[at] = zo_float_to_half(cf);
+            else if (Ctype == ZO_R_16BF) ((uint16_t *)C)[at] = zo_float_to_bf16(cf);
+            else ((float *)C)[at] = cf;
+        }
+    }
+    return ZO_OK;
+}
+
+/* The type/compute dispatch of cublasGemmEx (zblas/zblas.c:357-391), with
+ * the int8 branch added.  alpha/beta are float* for 32F compute and
+ * int32_t* for 32I compute. */
+int zo_gemm_ex(int transa, int transb, int m, int n, int k, const void *alpha,
+               const void *A, int Atype, int lda, const void *B, int Btype,
+               int ldb, const void *beta, void *C, int Ctype, int ldc,
+               int computeType) {
+    if (Atype == ZO_R_8I && Btype == ZO_R_8I && Ctype == ZO_R_32I
+        && (computeType == ZO_COMPUTE_32I || computeType == ZO_R_32I)) {
+        gemm_i8(transa, transb, m, n, k, *(const int32_t *)alpha,
+                (const int8_t *)A, lda, (const int8_t *)B, ldb,
+                *(const int32_t *)beta, (int32_t *)C, ldc);
+        return ZO_OK;
+    }
+    if (computeType != ZO_R_32F && computeType != ZO_COMPUTE_32F)
+        return ZO_NOT_SUPPORTED;
+    float al = *(const float *)alpha, be = *(const float *)beta;
+    if (Atype == ZO_R_32F && Btype == ZO_R_32F && Ctype == ZO_R_32F) {
+        zo_sgemm(transa, transb, m, n, k, al, (const float *)A, lda,
+                 (const float *)B, ldb, be, (float *)C, ldc);
+        return ZO_OK;
+    }
+    if (Atype == ZO_R_16BF && Btype == ZO_R_16BF) {
+        /* gemm_ex_host(wide=1): C narrow iff Ctype is bf16, else fp32 */
+        int ct = Ctype == ZO_R_16BF ? ZO_R_16BF : ZO_R_32F;
+        return gemm_wide(transa, transb, m, n, k, al, A, Atype, lda, B, Btype,
+                         ldb, be, C, ct, ldc);
+    }
+    if (Atype == ZO_R_16F && Btype == ZO_R_16F) {
+        int ct = Ctype == ZO_R_16F ? ZO_R_16F : ZO_R_32F;
+        return gemm_wide(transa, transb, m, n, k, al, A, Atype, lda, B, Btype,
+                         ldb, be, C, ct, ldc);
+    }
+    return ZO_NOT_SUPPORTED;
+}
+
+static size_t zo_elem_size(int type) {
+    switch (type) {
+    case ZO_R_16F: case ZO_R_16BF: return 2;
+    case ZO_R_8I: return 1;
+    default: return 4;
+    }
+}
+
+/* zblas/zblas.c:491-511.  The reference's elem_size (:488-490) returns 4
+ * for every type that is not 16-bit; int8 is new here and uses 1. */
+int zo_gemm_strided_batched_ex(int transa, int transb, int m, int n, int k,
+                               const void *alpha, const void *A, int Atype,
+                               int lda, long long sA, const void *B, int Btype,
+                               int ldb, long long sB, const void *beta, void *C,
+                               int Ctype, int ldc, long long sC, int batch,
+                               int computeType) {
+    for (int b = 0; b < batch; b++) {
+        int rc = zo_gemm_ex(transa, transb, m, n, k, alpha,
+                            (const char *)A + (size_t)b * sA * zo_elem_size(Atype),
+                            Atype, lda,
+                            (const char *)B + (size_t)b * sB * zo_elem_size(Btype),
+                            Btype, ldb, beta,
+                            (char *)C + (size_t)b * sC * zo_elem_size(Ctype),
+                            Ctype, ldc, computeType);
+        if (rc) return rc;
+    }
+    return ZO_OK;
+}
+
+/* Selected entries of C = alpha*op(A)op(B) + beta*C0 (no write to C):
+ * out[t] for (rows[t], cols[t]), as fp64 before the final narrowing.  Used
+ * to check full-size GEMMs by sampling. */
+void zo_gemm_entries(int transa, int transb, int k, double alpha,
+                     const void *A, int Atype, int lda,
+                     const void *B, int Btype, int ldb, double beta,
+                     const void *C0, int Ctype, int ldc,
+                     const int64_t *rows, const int64_t *cols, int64_t count,
+                     double *out) {
+#pragma omp parallel for schedule(static)
+    for (int64_t t = 0; t < count; t++) {
+        int64_t i = rows[t], j = cols[t];
+        double acc = 0.0;
+        for (int l = 0; l < k; l++)
+            acc += load_elem(A, Atype, opidx(transa, i, l, lda))
+                 * load_elem(B, Btype, opidx(transb, l, j, ldb));
+        double c = alpha * acc;
+        if (beta != 0.0 && C0) c += beta * load_elem(C0, Ctype, i + j * (int64_t)ldc);
+        out[t] = c;
+    }
+}
+
+/* ---- attention ------------------------------------------------------ */
+
+typedef struct {
+    const void *q, *k, *v;
+    void *o;                       /* same element type as q/k/v */
+    float *lse;                    /* [batch, heads, sq] fp32, may be NULL */
+    int64_t qb, qh, qr, kb, kh, kr, vb, vh, vr, ob, oh, orr;  /* elements */
+    int batch, heads, kv_ratio, sq, sk, d;
+    float scale;
+    int causal, diag;
+    int elem;                      /* 0 = f16, 1 = bf16, 2 = f32 */
+} zo_attn_desc;
+
+static double ld_in(const void *p, int elem, int64_t at) {
+    if (elem == 0) return zo_half_to_float(((const uint16_t *)p)[at]);
+    if (elem == 1) return zo_bf16_to_float(((const uint16_t *)p)[at]);
+    return ((const float *)p)[at];
+}
+
+static double round_in(double x, int elem) {
+    if (elem == 0) return zo_half_to_float(zo_float_to_half((float)x));
+    if (elem == 1) return zo_bf16_to_float(zo_float_to_bf16((float)x));
+    return (float)x;
+}
+
+static void st_out(void *p, int elem, int64_t at, double x) {
+    if (elem == 0) ((uint16_t *)p)[at] = zo_float_to_half((float)x);
+    else if (elem == 1) ((uint16_t *)p)[at] = zo_float_to_bf16((float)x);
+    else ((float *)p)[at] = (float)x;
+}
+
+/* One query row.  `work` holds sk doubles; `acc` holds d doubles.
+ * Writes O (d elements) at the row's output address, and LSE if wanted.
+ * If o_row is non-NULL it receives the fp64 O row before rounding. */
+static void attn_row(const zo_attn_desc *p, int b, int h, int i,
+                     double *work, double *acc, double *o_row, double *lse_row) {
+    const int hk = h / p->kv_ratio;
+    const int64_t qoff = b * p->qb + h * p->qh + (int64_t)i * p->qr;
+    const int64_t koff = b * p->kb + hk * p->kh;
+    const int64_t voff = b * p->vb + hk * p->vh;
+    const int64_t ooff = b * p->ob + h * p->oh + (int64_t)i * p->orr;
+    double mx = -INFINITY;
+    for (int j = 0; j < p->sk; j++) {
+        double s = 0.0;
+        for (int t = 0; t < p->d; t++)
+            s += ld_in(p->q, p->elem, qoff + t)
+               * ld_in(p->k, p->elem, koff + (int64_t)j * p->kr + t);
+        s *= (double)p->scale;
+        if (p->causal && j > i + p->diag) s = -INFINITY;
+        work[j] = s;
+        if (s > mx) mx = s;
+    }
+    double sum = 0.0;
+    for (int t = 0; t < p->d; t++) acc[t] = 0.0;
+    for (int j = 0; j < p->sk; j++) {
+        double e = mx == -INFINITY ? 0.0 : exp(work[j] - mx);
+        sum += e;
+        if (e == 0.0) continue;
+        double pe = p->elem == 2 ? e : round_in(e, p->elem);
+        for (int t = 0; t < p->d; t++)
+            acc[t] += pe * ld_in(p->v, p->elem, voff + (int64_t)j * p->vr + t);
+    }
+    double inv = sum > 0.0 ? 1.0 / sum : 0.0;
+    for (int t = 0; t < p->d; t++) {
+        double o = acc[t] * inv;
+        if (o_row) o_row[t] = o;
+        if (p->o) st_out(p->o, p->elem, ooff + t, o);
+    }
+    double l = sum > 0.0 ? mx + log(sum) : -INFINITY;
+    if (lse_row) *lse_row = l;
+    if (p->lse)
+        p->lse[((int64_t)b * p->heads + h) * p->sq + i] = (float)l;
+}
+
+/* Full attention forward over every (batch, head, query). */
+int zo_attention(const zo_attn_desc *p) {
+    if (!p || p->d <= 0 || p->sk <= 0 || p->kv_ratio <= 0) return ZO_INVALID_VALUE;
+    const int64_t rows = (int64_t)p->batch * p->heads * p->sq;
+#pragma omp parallel
+    {
+        double *work = malloc(sizeof(double) * (size_t)p->sk);
+        double *acc = malloc(sizeof(double) * (size_t)p->d);
+#pragma omp for schedule(dynamic, 16)
+        for (int64_t r = 0; r < rows; r++) {
+            int i = (int)(r % p->sq);
+            int h = (int)((r / p->sq) % p->heads);
+            int b = (int)(r / ((int64_t)p->sq * p->heads));
+            attn_row(p, b, h, i, work, acc, NULL, NULL);
+        }
+        free(work);
+        free(acc);
+    }
+    return ZO_OK;
+}
+
+/* Selected query rows only: for each t, (bs[t], hs[t], is[t]); writes the
+ * fp64 O rows to o_rows[t*d ...] and the LSE to lse_rows[t].  Does not
+ * touch p->o or p->lse. */
+int zo_attention_rows(const zo_attn_desc *p, const int32_t *bs, const int32_t *hs,
+                      const int32_t *is, int64_t count, double *o_rows,
+                      double *lse_rows) {
+    if (!p || p->d <= 0 || p->sk <= 0 || p->kv_ratio <= 0) return ZO_INVALID_VALUE;
+    zo_attn_desc q = *p;
+    q.o = NULL;
+    q.lse = NULL;
+#pragma omp parallel
+    {
+        double *work = malloc(sizeof(double) * (size_t)q.sk);
+        double *acc = malloc(sizeof(double) * (size_t)q.d);
+#pragma omp for schedule(dynamic, 1)
+        for (int64_t t = 0; t < count; t++)
+            attn_row(&q, bs[t], hs[t], is[t], work, acc, o_rows + t * q.d,
+                     lse_rows + t);
+        free(work);
+        free(acc);
+    }
+    return ZO_OK;
+}
+
+int zo_attn_desc_size(void) { return (int)sizeof(zo_attn_desc); }

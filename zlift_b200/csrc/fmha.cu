@@ -1,0 +1,475 @@
+// fmha.cu -- fused flash-attention forward on the sm_100a tensor cores.
+//
+// Replaces the reference's fmha_run (zblas/zblas_gpu.cpp:892-1039): tiled
+// online softmax over key tiles, causal mask `key > query + diag` with
+// causal tile skipping (:932-934), P rounded to the input type before P.V,
+// O accumulated in fp32 and normalised once at the end.  Adds the fp32
+// log-sum-exp output the reference never writes.
+//
+// One CTA owns two 128-query tiles of one (batch, head) and walks the key
+// tiles (128 keys) they need.  Ten warps:
+//   warps 0-3   softmax for query tile 0, warps 4-7 for query tile 1:
+//               tcgen05.ld a row of S = Q.K^T from TMEM (one thread per
+//               query row), row max, exp2, row sum, write P (16-bit) back
+//               into the same TMEM columns, rescale O in TMEM when the
+//               running max grew by more than 2^8 (lazy rescaling: the
+//               final O / l uses the same stale max, so the result is
+//               exact), and at the end normalise O and store it with LSE.
+//   warp 8      TMA producer: Q tiles once, then K and V tiles into a
+//               two-stage ring.
+//   warp 9      MMA issuer (one thread): S_t = Q_t.K_j^T (both operands in
+//               shared memory) and O_t += P_t.V_j (P from TMEM, V in shared
+//               memory), alternating the two query tiles so that one
+//               tile's softmax overlaps the other tile's matrix products.
+// TMEM columns: S0 [0,128) S1 [128,256) O0 [256,256+D) O1 [256+D, 256+2D).
+#include "fmha.h"
+#include "gemm.h"
+#include "ptx.cuh"
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <atomic>
+#include <cmath>
+
+namespace zl {
+
+namespace {
+
+constexpr int BQ = 128;          // queries per tile
+constexpr int BKEY = 128;        // keys per tile
+constexpr int kThreads = 320;
+constexpr float kLazyLog2 = 8.0f;   // rescale O only when the max grows by > 2^8
+
+template <int D>
+struct FCfg {
+    static constexpr int BOXES = D / 64;                 // 128-byte column boxes per row
+    static constexpr int TILE_BYTES = 128 * D * 2;       // one Q, K or V tile
+    static constexpr int Q_OFF = 0;                      // two Q tiles
+    static constexpr int KV_OFF = 2 * TILE_BYTES;        // stage s: K at +2s*TILE, V after
+    static constexpr int STAGES = 2;
+    static constexpr int BAR_OFF = KV_OFF + STAGES * 2 * TILE_BYTES;
+    static constexpr int SMEM = BAR_OFF + 256 + 1024;
+    static constexpr uint32_t S_COL0 = 0, S_COL1 = 128;
+    static constexpr uint32_t O_COL0 = 256, O_COL1 = 256 + D;
+    static constexpr uint32_t TMEM_COLS = 512;
+};
+
+struct FParams {
+    int heads, kv_ratio, sq, sk;
+    int npairs, nkt;             // query-tile pairs, key tiles
+    long long bh_begin, bh_count;
+    long long ob, oh, orr;       // output strides (elements)
+    void* o;
+    float* lse;
+    float scale, scale_log2;
+    int causal, diag;
+};
+
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+template <bool BF16>
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+    if constexpr (BF16) {
+        __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+        return *reinterpret_cast<uint32_t*>(&v);
+    } else {
+        __half2 v = __floats2half2_rn(a, b);
+        return *reinterpret_cast<uint32_t*>(&v);
+    }
+}
+
+// number of key tiles query tile [q0, q0+128) needs
+__device__ __forceinline__ int key_tiles(const FParams& p, int q0) {
+    if (q0 >= p.sq) return 0;
+    if (!p.causal) return p.nkt;
+    const int last_q = min(q0 + BQ - 1, p.sq - 1);
+    const int last_key = last_q + p.diag;
+    if (last_key < 0) return 0;
+    return min(last_key / BKEY + 1, p.nkt);
+}
+
+template <int D, bool BF16>
+__global__ void __launch_bounds__(kThreads, 1)
+fmha_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
+                const __grid_constant__ CUtensorMap tmK,
+                const __grid_constant__ CUtensorMap tmV,
+                const FParams p) {
+    using C = FCfg<D>;
+    constexpr uint32_t IDESC_QK = make_idesc(1, BF16 ? 1 : 0, 0, 0, BQ, BKEY);
+    constexpr uint32_t IDESC_PV = make_idesc(1, BF16 ? 1 : 0, 0, 1, BQ, D);
+    constexpr int BOX_BYTES = 128 * 128;                 // 128 rows x 128 bytes
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
+    uint64_t* qfull = bars + 0;
+    uint64_t* kfull = bars + 1;       // [2]
+    uint64_t* vfull = bars + 3;       // [2]
+    uint64_t* kvempty = bars + 5;     // [2]
+    uint64_t* sfull = bars + 7;       // [2] per query tile
+    uint64_t* pready = bars + 9;      // [2]
+    uint64_t* ofinal = bars + 11;     // [2]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    // heavy (late) query tiles first: blocks are dispatched in index order
+    const long long nbh = p.bh_count;
+    const int pair = p.npairs - 1 - (int)(blockIdx.x / nbh);
+    const long long bh = p.bh_begin + (long long)(blockIdx.x % nbh);
+    const int b = (int)(bh / p.heads), h = (int)(bh % p.heads);
+    const int hk = h / p.kv_ratio;
+    const int q0[2] = {pair * 2 * BQ, pair * 2 * BQ + BQ};
+    const int nt[2] = {key_tiles(p, q0[0]), key_tiles(p, q0[1])};
+    const int nmax = max(nt[0], nt[1]);
+
+    if (threadIdx.x == 0) {
+        mbar_init(qfull, 1);
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&kfull[i], 1);
+            mbar_init(&vfull[i], 1);
+            mbar_init(&kvempty[i], 1);
+            mbar_init(&sfull[i], 1);
+            mbar_init(&pready[i], 4);
+            mbar_init(&ofinal[i], 1);
+        }
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 9) {
+        tmem_alloc(tmem_slot, C::TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 8) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0 && nmax > 0) {
+            prefetch_tmap(&tmQ);
+            prefetch_tmap(&tmK);
+            prefetch_tmap(&tmV);
+            mbar_expect_tx(qfull, 2 * C::TILE_BYTES);
+            for (int t = 0; t < 2; t++)
+                for (int x = 0; x < C::BOXES; x++)
+                    tma_load_4d(smem + C::Q_OFF + t * C::TILE_BYTES + x * BOX_BYTES, &tmQ, qfull,
+                                x * 64, q0[t], h, b);
+            for (int j = 0; j < nmax; j++) {
+                const int st = j & 1;
+                if (!mbar_wait(&kvempty[st], ((j >> 1) & 1) ^ 1u, abort_flag)) break;
+                uint8_t* kt = smem + C::KV_OFF + st * 2 * C::TILE_BYTES;
+                uint8_t* vt = kt + C::TILE_BYTES;
+                mbar_expect_tx(&kfull[st], C::TILE_BYTES);
+                for (int x = 0; x < C::BOXES; x++)
+                    tma_load_4d(kt + x * BOX_BYTES, &tmK, &kfull[st], x * 64, j * BKEY, hk, b);
+                mbar_expect_tx(&vfull[st], C::TILE_BYTES);
+                for (int x = 0; x < C::BOXES; x++)
+                    tma_load_4d(vt + x * BOX_BYTES, &tmV, &vfull[st], x * 64, j * BKEY, hk, b);
+            }
+        }
+    } else if (warp == 9) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0 && nmax > 0) {
+            const uint32_t sq_base = smem_u32(smem + C::Q_OFF);
+            const uint32_t scol[2] = {C::S_COL0, C::S_COL1};
+            const uint32_t ocol[2] = {C::O_COL0, C::O_COL1};
+            auto issue_qk = [&](int t, int j) {
+                const uint32_t kb = smem_u32(smem + C::KV_OFF + (j & 1) * 2 * C::TILE_BYTES);
+                const uint32_t qb = sq_base + t * C::TILE_BYTES;
+#pragma unroll
+                for (int ks = 0; ks < D / 16; ks++) {
+                    const uint32_t off = (ks >> 2) * BOX_BYTES + (ks & 3) * 32;
+                    mma_f16_ss(tmem_base + scol[t], sw128_desc(qb + off, 16, 1024),
+                               sw128_desc(kb + off, 16, 1024), IDESC_QK, ks > 0 ? 1u : 0u);
+                }
+                mma_commit(&sfull[t]);
+            };
+            auto issue_pv = [&](int t, int j) {
+                const uint32_t vb =
+                    smem_u32(smem + C::KV_OFF + (j & 1) * 2 * C::TILE_BYTES + C::TILE_BYTES);
+#pragma unroll
+                for (int ks = 0; ks < BKEY / 16; ks++) {
+                    // P: 16 keys = 8 packed TMEM columns per step; V: 16 key rows
+                    mma_f16_ts(tmem_base + ocol[t], tmem_base + scol[t] + ks * 8,
+                               sw128_desc(vb + ks * 16 * 128, BOX_BYTES, 1024), IDESC_PV,
+                               (j > 0 || ks > 0) ? 1u : 0u);
+                }
+            };
+            bool ok = mbar_wait(qfull, 0, abort_flag) && mbar_wait(&kfull[0], 0, abort_flag);
+            if (ok) {
+                tc_fence_after();
+                for (int t = 0; t < 2; t++)
+                    if (nt[t] > 0) issue_qk(t, 0);
+            }
+            for (int j = 0; ok && j < nmax; j++) {
+                const int st = j & 1;
+                const uint32_t kv_par = (j >> 1) & 1;
+                if (!mbar_wait(&vfull[st], kv_par, abort_flag)) break;
+                const bool next_k = j + 1 < nmax;
+                bool have_next_k = false;
+                for (int t = 0; t < 2; t++) {
+                    if (j >= nt[t]) continue;
+                    if (!mbar_wait(&pready[t], j & 1, abort_flag)) { ok = false; break; }
+                    tc_fence_after();
+                    issue_pv(t, j);
+                    if (j + 1 == nt[t]) mma_commit(&ofinal[t]);
+                    if (j + 1 < nt[t]) {
+                        if (!have_next_k) {
+                            if (!mbar_wait(&kfull[(j + 1) & 1], ((j + 1) >> 1) & 1, abort_flag)) {
+                                ok = false;
+                                break;
+                            }
+                            tc_fence_after();
+                            have_next_k = true;
+                        }
+                        issue_qk(t, j + 1);
+                    }
+                }
+                (void)next_k;
+                mma_commit(&kvempty[st]);
+            }
+        }
+    } else {
+        // ---------------- softmax + epilogue (warps 0-7) ----------------
+        const int t = warp >> 2;
+        const int quarter = warp & 3;
+        const int r = quarter * 32 + lane;
+        const int qrow = q0[t] + r;
+        const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+        const uint32_t s_addr = tmem_base + lane_off + (t ? C::S_COL1 : C::S_COL0);
+        const uint32_t o_addr = tmem_base + lane_off + (t ? C::O_COL1 : C::O_COL0);
+        const float c = p.scale_log2;
+        float m_used = -INFINITY, l = 0.f;
+        bool alive = true;
+        for (int j = 0; j < nt[t]; j++) {
+            if (!mbar_wait(&sfull[t], j & 1, abort_flag)) { alive = false; break; }
+            tc_fence_after();
+            float s[BKEY];
+#pragma unroll
+            for (int c0 = 0; c0 < BKEY; c0 += 32)
+                tmem_ld32(s_addr + c0, *reinterpret_cast<uint32_t(*)[32]>(&s[c0]));
+            tmem_wait_ld();
+            const int key0 = j * BKEY;
+            const bool edge = (key0 + BKEY > p.sk) || (p.causal && key0 + BKEY - 1 > q0[t] + p.diag);
+            if (edge) {
+                const int lim = p.causal ? min(p.sk - 1, qrow + p.diag) : p.sk - 1;
+#pragma unroll
+                for (int i = 0; i < BKEY; i++)
+                    if (key0 + i > lim) s[i] = -INFINITY;
+            }
+            float mx = s[0];
+#pragma unroll
+            for (int i = 1; i < BKEY; i++) mx = fmaxf(mx, s[i]);
+            const float m_new = fmaxf(m_used, mx);
+            if (j == 0) {
+                m_used = m_new;
+            } else {
+                const bool resc = m_new != -INFINITY &&
+                                  (m_used == -INFINITY || (m_new - m_used) * c > kLazyLog2);
+                if (__any_sync(0xffffffffu, resc)) {
+                    const float alpha = resc ? ex2((m_used - m_new) * c) : 1.f;
+                    if (resc) {
+                        l *= alpha;
+                        m_used = m_new;
+                    }
+#pragma unroll 1
+                    for (int c0 = 0; c0 < D; c0 += 16) {
+                        uint32_t o[16];
+                        tmem_ld16(o_addr + c0, o);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 16; i++)
+                            o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+                        tmem_st16(o_addr + c0, o);
+                    }
+                }
+            }
+            const float mc = m_used == -INFINITY ? 0.f : m_used * c;
+            float sum = 0.f;
+            uint32_t pk[BKEY / 2];
+#pragma unroll
+            for (int i = 0; i < BKEY / 2; i++) {
+                const float p0 = ex2(fmaf(s[2 * i], c, -mc));
+                const float p1 = ex2(fmaf(s[2 * i + 1], c, -mc));
+                sum += p0 + p1;
+                pk[i] = pack2<BF16>(p0, p1);
+            }
+            l += sum;
+#pragma unroll
+            for (int c0 = 0; c0 < BKEY / 2; c0 += 16)
+                tmem_st16(s_addr + c0, *reinterpret_cast<uint32_t(*)[16]>(&pk[c0]));
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&pready[t]);
+        }
+        // ---- epilogue: O / l -> 16-bit, LSE ----
+        bool have_o = nt[t] > 0 && alive;
+        if (have_o) {
+            if (!mbar_wait(&ofinal[t], 0, abort_flag)) have_o = false;
+            else tc_fence_after();
+        }
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        const bool row_ok = qrow < p.sq;
+        typedef uint16_t u16;
+        u16* orow = static_cast<u16*>(p.o) + (long long)b * p.ob + (long long)h * p.oh +
+                    (long long)qrow * p.orr;
+#pragma unroll 1
+        for (int c0 = 0; c0 < D; c0 += 32) {
+            uint32_t v[32];
+            if (have_o) {
+                tmem_ld32(o_addr + c0, v);
+                tmem_wait_ld();
+            } else {
+#pragma unroll
+                for (int i = 0; i < 32; i++) v[i] = 0u;
+            }
+            if (row_ok) {
+                uint32_t w[16];
+#pragma unroll
+                for (int i = 0; i < 16; i++)
+                    w[i] = pack2<BF16>(__uint_as_float(v[2 * i]) * inv,
+                                       __uint_as_float(v[2 * i + 1]) * inv);
+                uint4* dst = reinterpret_cast<uint4*>(orow + c0);
+#pragma unroll
+                for (int i = 0; i < 4; i++)
+                    dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+            }
+        }
+        if (row_ok && p.lse) {
+            const float lse = l > 0.f ? m_used * p.scale + logf(l) : -INFINITY;
+            p.lse[bh * (long long)p.sq + qrow] = lse;
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 9) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, C::TMEM_COLS);
+    }
+}
+
+using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                              const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                              const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                              CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeFn encode_fn() {
+    static std::atomic<EncodeFn> fn{nullptr};
+    EncodeFn f = fn.load();
+    if (f) return f;
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess && q == cudaDriverEntryPointSuccess) {
+        f = reinterpret_cast<EncodeFn>(ptr);
+        fn.store(f);
+    }
+    return f;
+}
+
+// [batch][seq][heads][d] view of one operand: dims {d, seq, heads, batch}
+bool attn_tmap(CUtensorMap* tm, int elem, const void* base, int d, int seq, int heads,
+               int batch, long long rs, long long hs, long long bs) {
+    EncodeFn enc = encode_fn();
+    if (!enc) return false;
+    cuuint64_t dims[4] = {(cuuint64_t)d, (cuuint64_t)seq, (cuuint64_t)heads, (cuuint64_t)batch};
+    auto fix = [](long long s) { return (cuuint64_t)(s * 2 > 0 ? s * 2 : 16); };
+    cuuint64_t strides[3] = {fix(rs), fix(hs), fix(bs)};
+    cuuint32_t box[4] = {64, 128, 1, 1};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = enc(tm, elem == 1 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                     4, const_cast<void*>(base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+template <int D, bool BF16>
+int launch(const AttnDesc& d, const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v,
+           const FParams& p, long long grid, cudaStream_t s) {
+    using C = FCfg<D>;
+    auto kern = fmha_fwd_kernel<D, BF16>;
+    static std::atomic<unsigned long long> attr_set{0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const unsigned long long bit = 1ull << (dev & 63);
+    if (!(attr_set.load() & bit)) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+        if (e != cudaSuccess) return (int)e;
+        attr_set.fetch_or(bit);
+    }
+    kern<<<(unsigned)grid, kThreads, C::SMEM, s>>>(q, k, v, p);
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) note_launch();
+    return e == cudaSuccess ? 0 : (int)e;
+}
+
+bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+int fmha_fwd(const AttnDesc& d, cudaStream_t s) {
+    if (d.elem != 0 && d.elem != 1) return 1;
+    if (d.d != 64 && d.d != 128) return 1;
+    if (d.batches <= 0 || d.heads <= 0 || d.sq <= 0 || d.sk <= 0 || d.kv_ratio <= 0) return 1;
+    if (d.heads % d.kv_ratio) return 1;
+    if (!al16(d.q) || !al16(d.k) || !al16(d.v) || !al16(d.o)) return 1;
+    // TMA strides: multiples of 16 bytes; output rows written as 16-byte vectors
+    for (long long st : {d.qr, d.qh, d.qb, d.kr, d.kh, d.kb, d.vr, d.vh, d.vb})
+        if ((st * 2) % 16) return 1;
+    if ((d.orr * 2) % 16 || (d.oh * 2) % 16 || (d.ob * 2) % 16) return 1;
+    if (d.qr <= 0 || d.kr <= 0 || d.vr <= 0) return 1;
+    const int hk = d.heads / d.kv_ratio;
+    CUtensorMap tq, tk, tv;
+    if (!attn_tmap(&tq, d.elem, d.q, d.d, d.sq, d.heads, d.batches, d.qr, d.qh, d.qb)) return 1;
+    if (!attn_tmap(&tk, d.elem, d.k, d.d, d.sk, hk, d.batches, d.kr, d.kh, d.kb)) return 1;
+    if (!attn_tmap(&tv, d.elem, d.v, d.d, d.sk, hk, d.batches, d.vr, d.vh, d.vb)) return 1;
+    FParams p;
+    p.heads = d.heads;
+    p.kv_ratio = d.kv_ratio;
+    p.sq = d.sq;
+    p.sk = d.sk;
+    p.npairs = (d.sq + 2 * BQ - 1) / (2 * BQ);
+    p.nkt = (d.sk + BKEY - 1) / BKEY;
+    const long long total_bh = (long long)d.batches * d.heads;
+    p.bh_begin = d.pair_end > 0 ? d.pair_begin : 0;
+    p.bh_count = d.pair_end > 0 ? d.pair_end - d.pair_begin : total_bh;
+    if (p.bh_count <= 0) return 0;
+    p.ob = d.ob; p.oh = d.oh; p.orr = d.orr;
+    p.o = d.o;
+    p.lse = d.lse;
+    p.scale = d.scale;
+    p.scale_log2 = d.scale * 1.4426950408889634f;
+    p.causal = d.causal ? 1 : 0;
+    p.diag = d.diag;
+    const long long grid = (long long)p.npairs * p.bh_count;
+    if (grid > 0x7fffffffLL) return 1;
+    if (d.d == 128)
+        return d.elem == 1 ? launch<128, true>(d, tq, tk, tv, p, grid, s)
+                           : launch<128, false>(d, tq, tk, tv, p, grid, s);
+    return d.elem == 1 ? launch<64, true>(d, tq, tk, tv, p, grid, s)
+                       : launch<64, false>(d, tq, tk, tv, p, grid, s);
+}
+
+int fmha_error(bool clear) {
+    int v = 0;
+    cudaMemcpyFromSymbol(&v, g_dev_error, sizeof(int));
+    if (clear && v) {
+        int z = 0;
+        cudaMemcpyToSymbol(g_dev_error, &z, sizeof(int));
+    }
+    return v;
+}
+
+}  // namespace zl

@@ -1,0 +1,80 @@
+// gemm.h -- internal interface between the cuBLAS-style C ABI
+// (cublas_api.cpp) and the GEMM kernels (gemm_tc.cu, gemm_simt.cu).
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace zl {
+
+// cudaDataType_t values used at the boundary (same numbers as CUDA's).
+enum DType : int {
+    kR32F = 0,
+    kR16F = 2,
+    kR8I = 3,
+    kR32I = 10,
+    kR16BF = 14,
+};
+
+// How the tensor cores consume the inputs.
+enum class Kind : int {
+    F16 = 0,      // kind::f16, fp16 inputs
+    BF16 = 1,     // kind::f16, bf16 inputs
+    TF32X3 = 2,   // fp32 inputs as hi+lo tf32 planes, 3 products
+    TF32 = 3,     // fp32 inputs, one tf32 product (CUBLAS_TF32_TENSOR_OP_MATH)
+    I8 = 4,       // kind::i8, int32 accumulate
+};
+
+// One (possibly batched) column-major GEMM:
+//   C[b] = alpha * op(A[b]) * op(B[b]) + beta * C[b],  b < batch.
+// Strides and leading dimensions are in elements.  alpha/beta are read
+// from the host values unless the *_dev pointers are set (device pointer
+// mode), in which case the kernel dereferences them.
+struct GemmDesc {
+    int transa, transb;          // 0 = N, 1 = T (2 = C is treated as T)
+    int m, n, k, batch;
+    const void* A; long long lda, strideA; int Atype;
+    const void* B; long long ldb, strideB; int Btype;
+    void* C; long long ldc, strideC; int Ctype;
+    Kind kind;
+    float alpha, beta;           // 32F compute
+    int32_t ialpha, ibeta;       // 32I compute
+    const void* alpha_dev;       // device pointer mode (float* or int32_t*)
+    const void* beta_dev;
+    // fp32 split planes for Kind::TF32X3: hi and lo copies of A and B with
+    // the same layout as A and B.  Filled by the caller through split_tf32.
+    const float* A_lo; const float* B_lo;
+    const float* A_hi; const float* B_hi;
+};
+
+// Tensor-core path.  Returns 0 when launched, 1 when this shape/layout is
+// not eligible (the caller then uses the general kernel), or a CUDA error
+// code (> 1) on a launch failure.
+int gemm_tc(const GemmDesc& d, cudaStream_t s);
+
+// General CUDA-core kernel: any shape, any leading dimension, any alignment.
+int gemm_simt(const GemmDesc& d, cudaStream_t s);
+
+// Split an fp32 operand into K-major tf32 planes hi = rn(x), lo = rn(x - hi)
+// (round to nearest, ties away, to tf32's 10 mantissa bits).  Element
+// (mn, l), mn < MN, l < K, is read from X[b*stride + (k_contig ? mn*ld + l :
+// l*ld + mn)] and written to plane[b*MN*kp + mn*kp + l]; columns K..kp-1
+// are zero.  lo may be null (one-product tf32 mode).
+int split_tf32(const float* X, bool k_contig, long long MN, long long K, long long ld,
+               long long stride, int batch, long long kp, float* hi, float* lo,
+               cudaStream_t s);
+
+int num_sms();
+
+// Count of kernels this library has launched (all devices, all streams).
+void note_launch(unsigned n = 1);
+unsigned long long launch_count();
+
+// Device error words of the kernel translation units (read, optionally clear).
+int gemm_tc_error(bool clear);
+int gemm_simt_error(bool clear);
+int fmha_error(bool clear);
+
+// Trace switch (ZBLAS_TRACE set in the environment).
+bool tracing();
+
+}  // namespace zl

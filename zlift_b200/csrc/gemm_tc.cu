@@ -1,0 +1,567 @@
+// gemm_tc.cu -- column-major GEMM on the sm_100a tensor cores.
+//
+// Replaces the reference's XMX GEMMs (zblas/zblas_gpu.cpp: mad_h :405-497
+// for 16-bit inputs, mad :266-332 with split_to_bf16 :219-265 for fp32) and
+// adds the int8 x int8 -> int32 path the reference lacks.
+//
+// One persistent CTA per SM walks output tiles of 128 x BN (rows of C x
+// columns of C).  Six warps, each with one job:
+//   warp 0      TMA producer: loads 128-byte-swizzled A and B tiles into a
+//               STAGES-deep shared-memory ring (full/empty mbarriers).
+//   warp 1      MMA issuer: allocates TMEM, issues tcgen05.mma from one
+//               thread into one of two TMEM accumulators, and commits each
+//               stage back to the producer and each finished tile to the
+//               epilogue.
+//   warps 2-5   epilogue: tcgen05.ld the accumulator (warp w reads TMEM
+//               lanes 32*(w%4)..+31, i.e. rows of the tile), apply
+//               alpha*acc + beta*C, convert, store to C.  The two TMEM
+//               accumulators let the epilogue of tile i overlap the main
+//               loop of tile i+1.
+// Column-major operands need no staging transpose (the reference's
+// stage_tight, zblas_gpu.cpp:633-669): an operand whose contiguous
+// dimension is M or N is described to the tensor core as "MN-major".
+#include "gemm.h"
+#include "ptx.cuh"
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <atomic>
+#include <cstdio>
+#include <cstdlib>
+#include <mutex>
+
+namespace zl {
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int kThreads = 192;
+constexpr int kSmemBudget = 227 * 1024;     // dynamic shared memory per CTA
+constexpr int kSmemReserve = 1024 + 256;    // alignment slack + barriers
+
+template <int KIND> struct KT;
+template <> struct KT<(int)Kind::F16>    { static constexpr int es = 2, uk = 16, cfmt = 1, abfmt = 0, planes = 1; };
+template <> struct KT<(int)Kind::BF16>   { static constexpr int es = 2, uk = 16, cfmt = 1, abfmt = 1, planes = 1; };
+template <> struct KT<(int)Kind::TF32X3> { static constexpr int es = 4, uk = 8,  cfmt = 1, abfmt = 2, planes = 2; };
+template <> struct KT<(int)Kind::TF32>   { static constexpr int es = 4, uk = 8,  cfmt = 1, abfmt = 2, planes = 1; };
+template <> struct KT<(int)Kind::I8>     { static constexpr int es = 1, uk = 32, cfmt = 2, abfmt = 1, planes = 1; };
+
+struct TcParams {
+    int m, n, k, batch;
+    int tiles_m, tiles_n, k_blocks;
+    long long ldc, strideC;
+    void* C;
+    int out_type;
+    float alpha, beta;
+    int32_t ialpha, ibeta;
+    const void* alpha_dev;
+    const void* beta_dev;
+};
+
+template <int BN, int STAGES_OVERRIDE, int KIND>
+struct Cfg {
+    static constexpr int es = KT<KIND>::es;
+    static constexpr int BK = 128 / es;          // K elements per stage (one 128-byte row)
+    static constexpr int BOX = 128 / es;         // MN elements in one 128-byte row
+    static constexpr int A_BYTES = BM * 128;
+    static constexpr int B_BYTES = BN * 128;
+    static constexpr int PLANES = KT<KIND>::planes;
+    static constexpr int STAGE_BYTES = (A_BYTES + B_BYTES) * PLANES;
+    static constexpr int STAGES_FIT = (kSmemBudget - kSmemReserve) / STAGE_BYTES;
+    static constexpr int STAGES = STAGES_OVERRIDE > 0 ? STAGES_OVERRIDE
+                                : (STAGES_FIT > 8 ? 8 : STAGES_FIT);
+    static constexpr int TMEM_COLS = (2 * BN) < 32 ? 32 : (2 * BN);
+    static constexpr int SMEM = STAGES * STAGE_BYTES + kSmemReserve;
+};
+
+// Tile index -> (batch, tile row, tile column), walking groups of 8 tile
+// rows so that consecutive CTAs share B columns in L2 (the role of the
+// reference's slab rasterisation, zblas_gpu.cpp:414-430 / :498-504).
+__device__ __forceinline__ void decode_tile(int t, int tiles_m, int tiles_n,
+                                            int& b, int& tm, int& tn) {
+    const int per_b = tiles_m * tiles_n;
+    b = t / per_b;
+    const int r = t - b * per_b;
+    constexpr int G = 8;
+    const int group = r / (G * tiles_n);
+    const int first = group * G;
+    const int gm = min(tiles_m - first, G);
+    const int rr = r - group * G * tiles_n;
+    tm = first + rr % gm;
+    tn = rr / gm;
+}
+
+// One operand tile (ROWS of M or N by BK of K) into shared memory.
+//  K-major:  tensor map dims {K, MN, batch}, one box {BK, ROWS, 1}; row r
+//            of the tile (128 bytes) lands at r*128, 16-byte chunks XORed
+//            with r%8 (128-byte swizzle).
+//  MN-major: tensor map dims {MN, K, batch}, ROWS/BOX boxes {BOX, BK, 1};
+//            box i holds MN elements [i*BOX, (i+1)*BOX) for all BK values
+//            of K, K row kk at kk*128 within the box.
+template <bool MN, int ROWS, int BK, int BOX>
+__device__ __forceinline__ void load_operand(uint8_t* dst, const CUtensorMap* tm,
+                                             uint64_t* bar, int mn0, int k0, int b) {
+    if constexpr (!MN) {
+        tma_load_3d(dst, tm, bar, k0, mn0, b);
+    } else {
+#pragma unroll
+        for (int i = 0; i < ROWS / BOX; i++)
+            tma_load_3d(dst + i * (BK * 128), tm, bar, mn0 + i * BOX, k0, b);
+    }
+}
+
+// Descriptor of K step `ks` (uk elements of K) of an operand tile.
+//  K-major:  8-row core groups 1024 bytes apart (SBO); the K step moves the
+//            start address along the 128-byte row.
+//  MN-major: 64/32/128-element MN blocks BK*128 bytes apart (LBO), 8-row K
+//            groups 1024 bytes apart (SBO); the K step skips uk rows.
+template <bool MN, int BK, int UK>
+__device__ __forceinline__ uint64_t operand_desc(uint32_t base, int ks) {
+    if constexpr (!MN) {
+        return sw128_desc(base + ks * 32, 16, 1024);
+    } else {
+        return sw128_desc(base + ks * UK * 128, BK * 128, 1024);
+    }
+}
+
+template <int OUT>
+__device__ __forceinline__ void store_out(void* C, long long at, uint32_t raw,
+                                          float alpha, float beta,
+                                          int32_t ia, int32_t ib) {
+    if constexpr (OUT == kR32I) {
+        int32_t* c = static_cast<int32_t*>(C) + at;
+        uint32_t v = (uint32_t)ia * raw;                 // two's-complement wrap
+        if (ib != 0) v += (uint32_t)ib * (uint32_t)(*c);
+        *c = (int32_t)v;
+    } else {
+        float acc = __uint_as_float(raw);
+        float v = alpha * acc;
+        if constexpr (OUT == kR32F) {
+            float* c = static_cast<float*>(C) + at;
+            if (beta != 0.0f) v = fmaf(beta, *c, v);
+            *c = v;
+        } else if constexpr (OUT == kR16F) {
+            __half* c = static_cast<__half*>(C) + at;
+            if (beta != 0.0f) v = fmaf(beta, __half2float(*c), v);
+            *c = __float2half_rn(v);
+        } else {
+            __nv_bfloat16* c = static_cast<__nv_bfloat16*>(C) + at;
+            if (beta != 0.0f) v = fmaf(beta, __bfloat162float(*c), v);
+            *c = __float2bfloat16_rn(v);
+        }
+    }
+}
+
+template <int KIND, int BN, bool A_MN, bool B_MN, int OUT>
+__global__ void __launch_bounds__(kThreads, 1)
+gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
+               const __grid_constant__ CUtensorMap tmB,
+               const __grid_constant__ CUtensorMap tmA2,
+               const __grid_constant__ CUtensorMap tmB2,
+               const TcParams p) {
+    using C_ = Cfg<BN, 0, KIND>;
+    constexpr int BK = C_::BK, BOX = C_::BOX, STAGES = C_::STAGES;
+    constexpr int A_BYTES = C_::A_BYTES, B_BYTES = C_::B_BYTES;
+    constexpr int STAGE_BYTES = C_::STAGE_BYTES;
+    constexpr int UK = KT<KIND>::uk;
+    constexpr int KSTEPS = BK / UK;
+    constexpr uint32_t IDESC =
+        make_idesc(KT<KIND>::cfmt, KT<KIND>::abfmt, A_MN ? 1 : 0, B_MN ? 1 : 0, BM, BN);
+    constexpr uint32_t TMEM_COLS = C_::TMEM_COLS;
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+    uint64_t* empty = full + STAGES;
+    uint64_t* tfull = empty + STAGES;
+    uint64_t* tempty = tfull + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; a++) {
+            mbar_init(&tfull[a], 1);
+            mbar_init(&tempty[a], 4);       // one arrival per epilogue warp
+        }
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0 && lane == 0) {
+        prefetch_tmap(&tmA);
+        prefetch_tmap(&tmB);
+        if constexpr (C_::PLANES == 2) {
+            prefetch_tmap(&tmA2);
+            prefetch_tmap(&tmB2);
+        }
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    const int total = p.tiles_m * p.tiles_n * p.batch;
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            for (int t = blockIdx.x; t < total; t += gridDim.x) {
+                int b, tm, tn;
+                decode_tile(t, p.tiles_m, p.tiles_n, b, tm, tn);
+                const int m0 = tm * BM, n0 = tn * BN;
+                for (int kb = 0; kb < p.k_blocks; kb++) {
+                    if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) goto producer_done;
+                    uint8_t* sa = smem + stage * STAGE_BYTES;
+                    uint8_t* sb = sa + A_BYTES;
+                    mbar_expect_tx(&full[stage], STAGE_BYTES);
+                    const int k0 = kb * BK;
+                    load_operand<A_MN, BM, BK, BOX>(sa, &tmA, &full[stage], m0, k0, b);
+                    load_operand<B_MN, BN, BK, BOX>(sb, &tmB, &full[stage], n0, k0, b);
+                    if constexpr (C_::PLANES == 2) {
+                        load_operand<A_MN, BM, BK, BOX>(sb + B_BYTES, &tmA2, &full[stage], m0, k0, b);
+                        load_operand<B_MN, BN, BK, BOX>(sb + B_BYTES + A_BYTES, &tmB2, &full[stage], n0, k0, b);
+                    }
+                    if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+                }
+            }
+        producer_done:;
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            int local = 0;
+            for (int t = blockIdx.x; t < total; t += gridDim.x, local++) {
+                const int acc = local & 1;
+                const uint32_t aphase = (local >> 1) & 1;
+                if (!mbar_wait(&tempty[acc], aphase ^ 1u, abort_flag)) break;
+                tc_fence_after();
+                const uint32_t d = tmem_base + acc * BN;
+                for (int kb = 0; kb < p.k_blocks; kb++) {
+                    if (!mbar_wait(&full[stage], phase, abort_flag)) goto mma_done;
+                    tc_fence_after();
+                    const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
+                    const uint32_t sb = sa + A_BYTES;
+#pragma unroll
+                    for (int ks = 0; ks < KSTEPS; ks++) {
+                        const uint64_t ad = operand_desc<A_MN, BK, UK>(sa, ks);
+                        const uint64_t bd = operand_desc<B_MN, BK, UK>(sb, ks);
+                        const uint32_t accum = (kb | ks) != 0 ? 1u : 0u;
+                        if constexpr (KIND == (int)Kind::TF32X3) {
+                            // small terms first: lo*hi, hi*lo, then hi*hi
+                            const uint64_t ad2 = operand_desc<A_MN, BK, UK>(sb + B_BYTES, ks);
+                            const uint64_t bd2 = operand_desc<B_MN, BK, UK>(sb + B_BYTES + A_BYTES, ks);
+                            mma_tf32_ss(d, ad2, bd, IDESC, accum);
+                            mma_tf32_ss(d, ad, bd2, IDESC, 1u);
+                            mma_tf32_ss(d, ad, bd, IDESC, 1u);
+                        } else if constexpr (KIND == (int)Kind::TF32) {
+                            mma_tf32_ss(d, ad, bd, IDESC, accum);
+                        } else if constexpr (KIND == (int)Kind::I8) {
+                            mma_i8_ss(d, ad, bd, IDESC, accum);
+                        } else {
+                            mma_f16_ss(d, ad, bd, IDESC, accum);
+                        }
+                    }
+                    mma_commit(&empty[stage]);
+                    if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+                }
+                mma_commit(&tfull[acc]);
+            }
+        mma_done:;
+        }
+    } else {
+        // ---------------- epilogue ----------------
+        const int q = warp & 3;                 // TMEM lane quarter of this warp
+        const int r_in_tile = q * 32 + lane;
+        float alpha = p.alpha, beta = p.beta;
+        int32_t ia = p.ialpha, ib = p.ibeta;
+        if (p.alpha_dev) {
+            if constexpr (OUT == kR32I) ia = *static_cast<const int32_t*>(p.alpha_dev);
+            else alpha = *static_cast<const float*>(p.alpha_dev);
+        }
+        if (p.beta_dev) {
+            if constexpr (OUT == kR32I) ib = *static_cast<const int32_t*>(p.beta_dev);
+            else beta = *static_cast<const float*>(p.beta_dev);
+        }
+        int local = 0;
+        for (int t = blockIdx.x; t < total; t += gridDim.x, local++) {
+            const int acc = local & 1;
+            const uint32_t aphase = (local >> 1) & 1;
+            if (!mbar_wait(&tfull[acc], aphase, abort_flag)) break;
+            tc_fence_after();
+            int b, tm, tn;
+            decode_tile(t, p.tiles_m, p.tiles_n, b, tm, tn);
+            const long long row = (long long)tm * BM + r_in_tile;
+            const bool row_ok = row < p.m;
+            const int n0 = tn * BN;
+            const long long base = (long long)b * p.strideC + row;
+            const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
+#pragma unroll 1
+            for (int c0 = 0; c0 < BN; c0 += 32) {
+                uint32_t v[32];
+                tmem_ld32(taddr + c0, v);
+                tmem_wait_ld();
+                if (row_ok) {
+#pragma unroll
+                    for (int j = 0; j < 32; j++) {
+                        const int col = n0 + c0 + j;
+                        if (col < p.n)
+                            store_out<OUT>(p.C, base + (long long)col * p.ldc, v[j],
+                                           alpha, beta, ia, ib);
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[acc]);
+        }
+    }
+
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, TMEM_COLS);
+    }
+}
+
+// ---------------- host side ----------------
+
+using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                              const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                              const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                              CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeFn encode_fn() {
+    static EncodeFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) ==
+                cudaSuccess && q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeFn>(f);
+    });
+    return fn;
+}
+
+CUtensorMapDataType tmap_type(Kind k) {
+    switch (k) {
+    case Kind::F16: return CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    case Kind::BF16: return CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    case Kind::I8: return CU_TENSOR_MAP_DATA_TYPE_UINT8;
+    default: return CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+    }
+}
+
+int elem_bytes(Kind k) {
+    switch (k) {
+    case Kind::F16: case Kind::BF16: return 2;
+    case Kind::I8: return 1;
+    default: return 4;
+    }
+}
+
+// Tensor map for one operand.  `inner`/`outer` are the logical extents of
+// the contiguous and strided dimensions, `ld` the stride between outer
+// indices and `stride` the batch stride (elements).
+bool make_tmap(CUtensorMap* tm, Kind kind, const void* base, long long inner,
+               long long outer, long long ld, long long stride, int batch,
+               int box_inner, int box_outer) {
+    EncodeFn enc = encode_fn();
+    if (!enc) return false;
+    const int es = elem_bytes(kind);
+    cuuint64_t dims[3] = {(cuuint64_t)inner, (cuuint64_t)outer, (cuuint64_t)batch};
+    long long bstride = batch > 1 ? stride : ld * outer;
+    if (bstride <= 0) bstride = ld * outer;
+    cuuint64_t strides[2] = {(cuuint64_t)(ld * es), (cuuint64_t)(bstride * es)};
+    // the batch stride of a single matrix is never used; keep it legal
+    if (batch == 1) strides[1] = (strides[1] + 15) & ~cuuint64_t(15);
+    cuuint32_t box[3] = {(cuuint32_t)box_inner, (cuuint32_t)box_outer, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = enc(tm, tmap_type(kind), 3, const_cast<void*>(base), dims, strides, box,
+                     estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+template <int KIND, int BN, bool A_MN, bool B_MN, int OUT>
+int launch(const GemmDesc& d, const CUtensorMap& a, const CUtensorMap& b,
+           const CUtensorMap& a2, const CUtensorMap& b2, const TcParams& p,
+           cudaStream_t s) {
+    using C_ = Cfg<BN, 0, KIND>;
+    auto kern = gemm_tc_kernel<KIND, BN, A_MN, B_MN, OUT>;
+    static std::atomic<unsigned long long> attr_set{0};   // one bit per device
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const unsigned long long bit = 1ull << (dev & 63);
+    if (!(attr_set.load() & bit)) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             C_::SMEM);
+        if (e != cudaSuccess) return (int)e;
+        attr_set.fetch_or(bit);
+    }
+    const int total = p.tiles_m * p.tiles_n * p.batch;
+    const int grid = total < num_sms() ? total : num_sms();
+    kern<<<grid, kThreads, C_::SMEM, s>>>(a, b, a2, b2, p);
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) note_launch();
+    return e == cudaSuccess ? 0 : (int)e;
+}
+
+template <int KIND, int BN, bool A_MN, bool B_MN>
+int launch_out(const GemmDesc& d, const CUtensorMap& a, const CUtensorMap& b,
+               const CUtensorMap& a2, const CUtensorMap& b2, const TcParams& p,
+               cudaStream_t s) {
+    switch (d.Ctype) {
+    case kR16F: return launch<KIND, BN, A_MN, B_MN, kR16F>(d, a, b, a2, b2, p, s);
+    case kR16BF: return launch<KIND, BN, A_MN, B_MN, kR16BF>(d, a, b, a2, b2, p, s);
+    case kR32F: return launch<KIND, BN, A_MN, B_MN, kR32F>(d, a, b, a2, b2, p, s);
+    default: return 1;
+    }
+}
+
+template <int KIND, int BN>
+int launch_major(const GemmDesc& d, bool a_mn, bool b_mn, const CUtensorMap& a,
+                 const CUtensorMap& b, const CUtensorMap& a2, const CUtensorMap& b2,
+                 const TcParams& p, cudaStream_t s) {
+    if constexpr (KIND == (int)Kind::I8) {
+        if (d.Ctype != kR32I) return 1;
+        if (a_mn && b_mn) return launch<KIND, BN, true, true, kR32I>(d, a, b, a2, b2, p, s);
+        if (a_mn) return launch<KIND, BN, true, false, kR32I>(d, a, b, a2, b2, p, s);
+        if (b_mn) return launch<KIND, BN, false, true, kR32I>(d, a, b, a2, b2, p, s);
+        return launch<KIND, BN, false, false, kR32I>(d, a, b, a2, b2, p, s);
+    } else if constexpr (KIND == (int)Kind::TF32X3 || KIND == (int)Kind::TF32) {
+        if (d.Ctype != kR32F) return 1;
+        if (a_mn && b_mn) return launch<KIND, BN, true, true, kR32F>(d, a, b, a2, b2, p, s);
+        if (a_mn) return launch<KIND, BN, true, false, kR32F>(d, a, b, a2, b2, p, s);
+        if (b_mn) return launch<KIND, BN, false, true, kR32F>(d, a, b, a2, b2, p, s);
+        return launch<KIND, BN, false, false, kR32F>(d, a, b, a2, b2, p, s);
+    } else {
+        if (a_mn && b_mn) return launch_out<KIND, BN, true, true>(d, a, b, a2, b2, p, s);
+        if (a_mn) return launch_out<KIND, BN, true, false>(d, a, b, a2, b2, p, s);
+        if (b_mn) return launch_out<KIND, BN, false, true>(d, a, b, a2, b2, p, s);
+        return launch_out<KIND, BN, false, false>(d, a, b, a2, b2, p, s);
+    }
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+int num_sms() {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    static int cache[64] = {0};
+    if (dev < 0 || dev >= 64) return 148;
+    if (!cache[dev]) {
+        int n = 0;
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        cache[dev] = n > 0 ? n : 148;
+    }
+    return cache[dev];
+}
+
+int gemm_tc(const GemmDesc& d, cudaStream_t s) {
+    if (getenv("ZBLAS_NO_TC")) return 1;
+    if (d.m <= 0 || d.n <= 0 || d.k <= 0 || d.batch <= 0) return 1;
+    const int es = elem_bytes(d.kind);
+    // TMA: 16-byte aligned bases, 16-byte multiple strides
+    const void* a_base = d.kind == Kind::TF32X3 ? (const void*)d.A_hi : d.A;
+    const void* b_base = d.kind == Kind::TF32X3 ? (const void*)d.B_hi : d.B;
+    if (!aligned16(a_base) || !aligned16(b_base)) return 1;
+    if (d.kind == Kind::TF32X3 && (!aligned16(d.A_lo) || !aligned16(d.B_lo))) return 1;
+    if ((d.lda * es) % 16 || (d.ldb * es) % 16) return 1;
+    if (d.batch > 1 && ((d.strideA * es) % 16 || (d.strideB * es) % 16)) return 1;
+    if (d.batch > 1 && (d.strideA <= 0 || d.strideB <= 0)) return 1;
+    if (d.k > (1 << 30) || d.m > (1 << 30) || d.n > (1 << 30)) return 1;
+
+    const bool a_mn = d.transa == 0;     // op(A)(i,l) = A[i + l*lda]: M contiguous
+    const bool b_mn = d.transb != 0;     // op(B)(l,j) = B[j + l*ldb]: N contiguous
+    const int bk = 128 / es, box = 128 / es;
+
+    // tile width: 256 columns when that still fills the GPU
+    const int sms = num_sms();
+    const long long tiles256 = (long long)((d.m + BM - 1) / BM) * ((d.n + 255) / 256) * d.batch;
+    int BN = 256;
+    if (d.kind == Kind::TF32X3) BN = 128;
+    else if (tiles256 < sms && d.n > 128) BN = 128;
+    else if (d.n <= 128) BN = 128;
+    if (d.kind == Kind::TF32X3) {
+        const long long tiles128 = (long long)((d.m + BM - 1) / BM) * ((d.n + 127) / 128) * d.batch;
+        if (tiles128 < sms) BN = 64;
+    }
+
+    CUtensorMap ta, tb, ta2, tb2;
+    auto mk = [&](CUtensorMap* tm, const void* base, bool mn, long long mn_ext, long long ld,
+                  long long stride, int rows) {
+        if (mn) return make_tmap(tm, d.kind, base, mn_ext, d.k, ld, stride, d.batch, box, bk);
+        return make_tmap(tm, d.kind, base, d.k, mn_ext, ld, stride, d.batch, bk, rows);
+    };
+    if (!mk(&ta, a_base, a_mn, d.m, d.lda, d.strideA, BM)) return 1;
+    if (!mk(&tb, b_base, b_mn, d.n, d.ldb, d.strideB, BN)) return 1;
+    if (d.kind == Kind::TF32X3) {
+        if (!mk(&ta2, d.A_lo, a_mn, d.m, d.lda, d.strideA, BM)) return 1;
+        if (!mk(&tb2, d.B_lo, b_mn, d.n, d.ldb, d.strideB, BN)) return 1;
+    } else {
+        ta2 = ta;
+        tb2 = tb;
+    }
+
+    TcParams p;
+    p.m = d.m; p.n = d.n; p.k = d.k; p.batch = d.batch;
+    p.tiles_m = (d.m + BM - 1) / BM;
+    p.tiles_n = (d.n + BN - 1) / BN;
+    p.k_blocks = (d.k + bk - 1) / bk;
+    p.ldc = d.ldc;
+    p.strideC = d.strideC;
+    p.C = d.C;
+    p.out_type = d.Ctype;
+    p.alpha = d.alpha; p.beta = d.beta;
+    p.ialpha = d.ialpha; p.ibeta = d.ibeta;
+    p.alpha_dev = d.alpha_dev; p.beta_dev = d.beta_dev;
+
+    switch (d.kind) {
+    case Kind::F16:
+        return BN == 256 ? launch_major<(int)Kind::F16, 256>(d, a_mn, b_mn, ta, tb, ta2, tb2, p, s)
+                         : launch_major<(int)Kind::F16, 128>(d, a_mn, b_mn, ta, tb, ta2, tb2, p, s);
+    case Kind::BF16:
+        return BN == 256 ? launch_major<(int)Kind::BF16, 256>(d, a_mn, b_mn, ta, tb, ta2, tb2, p, s)
+                         : launch_major<(int)Kind::BF16, 128>(d, a_mn, b_mn, ta, tb, ta2, tb2, p, s);
+    case Kind::I8:
+        return BN == 256 ? launch_major<(int)Kind::I8, 256>(d, a_mn, b_mn, ta, tb, ta2, tb2, p, s)
+                         : launch_major<(int)Kind::I8, 128>(d, a_mn, b_mn, ta, tb, ta2, tb2, p, s);
+    case Kind::TF32:
+        return BN == 256 ? launch_major<(int)Kind::TF32, 256>(d, a_mn, b_mn, ta, tb, ta2, tb2, p, s)
+                         : launch_major<(int)Kind::TF32, 128>(d, a_mn, b_mn, ta, tb, ta2, tb2, p, s);
+    case Kind::TF32X3:
+        return BN == 128 ? launch_major<(int)Kind::TF32X3, 128>(d, a_mn, b_mn, ta, tb, ta2, tb2, p, s)
+                         : launch_major<(int)Kind::TF32X3, 64>(d, a_mn, b_mn, ta, tb, ta2, tb2, p, s);
+    }
+    return 1;
+}
+
+int gemm_tc_error(bool clear) {
+    int v = 0;
+    cudaMemcpyFromSymbol(&v, g_dev_error, sizeof(int));
+    if (clear && v) {
+        int z = 0;
+        cudaMemcpyToSymbol(g_dev_error, &z, sizeof(int));
+    }
+    return v;
+}
+
+}  // namespace zl

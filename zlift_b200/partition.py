@@ -1,0 +1,85 @@
+"""Python side of the partition layer (include/zlift_partition.h).
+
+The shard arithmetic and the collective live in libcublas.so.13; this
+module only forwards to it.  `Comm` wraps an NCCL communicator created by
+the library; its 128-byte unique id travels over whatever channel the
+caller has (torch.distributed here).
+"""
+from __future__ import annotations
+
+import ctypes
+
+from . import load
+
+
+def shard_range(total: int, parts: int, index: int, align: int = 1) -> tuple[int, int]:
+    """[begin, end) of rank `index` of `parts` over `total` units, in
+    multiples of `align` (zlift_part_range)."""
+    b, e = ctypes.c_longlong(), ctypes.c_longlong()
+    rc = load().zlift_part_range(total, parts, index, align, ctypes.byref(b), ctypes.byref(e))
+    if rc:
+        raise ValueError(f"zlift_part_range({total}, {parts}, {index}, {align}) -> {rc}")
+    return b.value, e.value
+
+
+def flash_pairs(block, elem: int, pair_begin: int, pair_end: int, stream=None) -> int:
+    """Flash forward over (batch, head) pairs [pair_begin, pair_end)."""
+    s = 0 if stream is None else int(getattr(stream, "cuda_stream", stream))
+    return load().zlift_part_flash_fwd(ctypes.byref(block), ctypes.sizeof(block), elem,
+                                       pair_begin, pair_end, s)
+
+
+class Comm:
+    """NCCL communicator of the partition layer."""
+
+    def __init__(self, nranks: int, rank: int, unique_id: bytes):
+        self.lib = load()
+        c = ctypes.c_void_p()
+        buf = ctypes.create_string_buffer(unique_id, 128)
+        rc = self.lib.zlift_part_comm_init(ctypes.byref(c), nranks, rank, buf)
+        if rc:
+            raise RuntimeError(f"zlift_part_comm_init -> {rc}")
+        self.c, self.nranks, self.rank = c, nranks, rank
+
+    @staticmethod
+    def unique_id() -> bytes:
+        buf = ctypes.create_string_buffer(128)
+        rc = load().zlift_part_unique_id(buf)
+        if rc:
+            raise RuntimeError(f"zlift_part_unique_id -> {rc}")
+        return buf.raw
+
+    def wait(self, stream, timeout_ms: int = 10000) -> int:
+        s = int(getattr(stream, "cuda_stream", stream or 0))
+        return self.lib.zlift_part_comm_wait(self.c, s, timeout_ms)
+
+    def close(self):
+        if self.c:
+            self.lib.zlift_part_comm_destroy(self.c)
+            self.c = None
+
+
+def gemm_ex_nsplit(handle, comm, nranks, rank, transa, transb, m, n, k, alpha, A, Atype, lda,
+                   B_block, Btype, ldb, beta, C, Ctype, compute) -> int:
+    """N-split GEMM + all-gather (zlift_part_gemm_ex_nsplit)."""
+    from .blas import COMPUTE_32I, R_32I, _ptr
+    integer = compute in (COMPUTE_32I, R_32I)
+    al = ctypes.c_int32(int(alpha)) if integer else ctypes.c_float(float(alpha))
+    be = ctypes.c_int32(int(beta)) if integer else ctypes.c_float(float(beta))
+    return load().zlift_part_gemm_ex_nsplit(
+        handle.h, comm.c if comm is not None else None, nranks, rank, transa, transb, m, n, k,
+        ctypes.byref(al), _ptr(A), Atype, lda, _ptr(B_block), Btype, ldb, ctypes.byref(be),
+        _ptr(C), Ctype, compute)
+
+
+def gemm_strided_batched_range(handle, batch_begin, batch_end, transa, transb, m, n, k, alpha,
+                               A, Atype, lda, sA, B, Btype, ldb, sB, beta, C, Ctype, ldc, sC,
+                               compute) -> int:
+    from .blas import COMPUTE_32I, R_32I, _ptr
+    integer = compute in (COMPUTE_32I, R_32I)
+    al = ctypes.c_int32(int(alpha)) if integer else ctypes.c_float(float(alpha))
+    be = ctypes.c_int32(int(beta)) if integer else ctypes.c_float(float(beta))
+    return load().zlift_part_gemm_strided_batched_ex(
+        handle.h, batch_begin, batch_end, transa, transb, m, n, k, ctypes.byref(al), _ptr(A),
+        Atype, lda, sA, _ptr(B), Btype, ldb, sB, ctypes.byref(be), _ptr(C), Ctype, ldc, sC,
+        compute)
