@@ -125,30 +125,36 @@ __device__ __forceinline__ uint64_t operand_desc(uint32_t base, int ks) {
     }
 }
 
+// Raw bits of C's old value (for beta * C), read ahead of the stores.
 template <int OUT>
-__device__ __forceinline__ void store_out(void* C, long long at, uint32_t raw,
-                                          float alpha, float beta,
+__device__ __forceinline__ uint32_t load_c(const void* C, long long at) {
+    if constexpr (OUT == kR16F || OUT == kR16BF)
+        return static_cast<const uint16_t*>(C)[at];
+    else
+        return static_cast<const uint32_t*>(C)[at];
+}
+
+// alpha * acc + beta * old, converted to the output type and stored.
+template <int OUT>
+__device__ __forceinline__ void store_out(void* C, long long at, uint32_t raw, uint32_t old,
+                                          bool use_beta, float alpha, float beta,
                                           int32_t ia, int32_t ib) {
     if constexpr (OUT == kR32I) {
-        int32_t* c = static_cast<int32_t*>(C) + at;
         uint32_t v = (uint32_t)ia * raw;                 // two's-complement wrap
-        if (ib != 0) v += (uint32_t)ib * (uint32_t)(*c);
-        *c = (int32_t)v;
+        if (use_beta) v += (uint32_t)ib * old;
+        static_cast<int32_t*>(C)[at] = (int32_t)v;
     } else {
-        float acc = __uint_as_float(raw);
-        float v = alpha * acc;
+        float v = alpha * __uint_as_float(raw);
         if constexpr (OUT == kR32F) {
-            float* c = static_cast<float*>(C) + at;
-            if (beta != 0.0f) v = fmaf(beta, *c, v);
-            *c = v;
+            if (use_beta) v = fmaf(beta, __uint_as_float(old), v);
+            static_cast<float*>(C)[at] = v;
         } else if constexpr (OUT == kR16F) {
-            __half* c = static_cast<__half*>(C) + at;
-            if (beta != 0.0f) v = fmaf(beta, __half2float(*c), v);
-            *c = __float2half_rn(v);
+            if (use_beta) v = fmaf(beta, __half2float(__ushort_as_half((unsigned short)old)), v);
+            static_cast<__half*>(C)[at] = __float2half_rn(v);
         } else {
-            __nv_bfloat16* c = static_cast<__nv_bfloat16*>(C) + at;
-            if (beta != 0.0f) v = fmaf(beta, __bfloat162float(*c), v);
-            *c = __float2bfloat16_rn(v);
+            if (use_beta)
+                v = fmaf(beta, __bfloat162float(__ushort_as_bfloat16((unsigned short)old)), v);
+            static_cast<__nv_bfloat16*>(C)[at] = __float2bfloat16_rn(v);
         }
     }
 }
@@ -310,20 +316,37 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
             const int n0 = tn * BN;
             const long long base = (long long)b * p.strideC + row;
             const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
+            const bool use_beta = OUT == kR32I ? ib != 0 : beta != 0.0f;
+            // beta * C: the old values of chunk c+1 are loaded while chunk c
+            // is converted and stored, so C's read latency is paid once per
+            // tile rather than once per column
+            uint32_t old[32], old_next[32];
+            auto fetch = [&](int c0, uint32_t (&dst)[32]) {
+#pragma unroll
+                for (int j = 0; j < 32; j++) {
+                    const int col = n0 + c0 + j;
+                    dst[j] = (use_beta && row_ok && col < p.n)
+                                 ? load_c<OUT>(p.C, base + (long long)col * p.ldc) : 0u;
+                }
+            };
+            fetch(0, old);
 #pragma unroll 1
             for (int c0 = 0; c0 < BN; c0 += 32) {
                 uint32_t v[32];
                 tmem_ld32(taddr + c0, v);
+                if (c0 + 32 < BN) fetch(c0 + 32, old_next);
                 tmem_wait_ld();
                 if (row_ok) {
 #pragma unroll
                     for (int j = 0; j < 32; j++) {
                         const int col = n0 + c0 + j;
                         if (col < p.n)
-                            store_out<OUT>(p.C, base + (long long)col * p.ldc, v[j],
-                                           alpha, beta, ia, ib);
+                            store_out<OUT>(p.C, base + (long long)col * p.ldc, v[j], old[j],
+                                           use_beta, alpha, beta, ia, ib);
                     }
                 }
+#pragma unroll
+                for (int j = 0; j < 32; j++) old[j] = old_next[j];
             }
             tc_fence_before();
             __syncwarp();
