@@ -137,6 +137,26 @@ ZLIFT_API cublasStatus_t cublasHgemm(cublasHandle_t handle, int transa, int tran
                            const unsigned short *beta, unsigned short *C,
                            int ldc);
 
+/* fp32 GEMM with the arguments and results of cublasSgemm_v2 that
+ * allocates no device memory.  No counterpart in the reference.
+ * For callers that must not call cudaMalloc: code inside a CUDA-graph
+ * capture that may not allocate, programs whose device memory is already
+ * fully reserved, and interposition layers (like zLift's, which answers a
+ * program's cuBLAS calls from inside that program) that must leave the
+ * program's allocations alone.  cublasSgemm_v2 keeps its tf32 split planes
+ * in scratch it allocates per handle; this entry keeps them in a fixed
+ * 16 MiB array of the library's device image (per GPU, held until exit).
+ * Limit: 4 * P * (m*kp + n*kp) bytes <= 16 MiB, kp = k rounded up to 4,
+ * P = 2 (default math) or 1 (CUBLAS_TF32_TENSOR_OP_MATH); larger calls
+ * return CUBLAS_STATUS_INVALID_VALUE.  The first call on a device looks up
+ * the array's address there -- make it before any stream capture.  All
+ * calls share the array: calls whose kernels overlap on the GPU race, so
+ * keep them on one stream. */
+ZLIFT_API cublasStatus_t zlift_sgemm_noalloc(cublasHandle_t handle, int transa, int transb,
+                                             int m, int n, int k, const float *alpha,
+                                             const float *A, int lda, const float *B, int ldb,
+                                             const float *beta, float *C, int ldc);
+
 /* ---- library extras (no reference counterpart) ------------------------ */
 
 /* Returns and clears the device error word: 0 if no kernel of this library

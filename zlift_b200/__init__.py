@@ -55,6 +55,9 @@ SIGNATURES = [
                               c_void_p, c_int, c_int]),
     ("cublasHgemm", c_int, [c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p,
                             c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_int]),
+    ("zlift_sgemm_noalloc", c_int, [c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p,
+                                    c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p,
+                                    c_int]),
     ("zlift_device_error", c_int, []),
     ("zlift_launch_count", ctypes.c_ulonglong, []),
     ("zblas_gpu_flash_f16", c_int, [c_void_p, c_uint, c_int]),

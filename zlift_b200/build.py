@@ -43,6 +43,7 @@ SOURCES = [
     "attention_api.cu",
     "cublas_api.cu",
     "partition.cu",
+    "noalloc.cu",
 ]
 
 
