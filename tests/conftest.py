@@ -12,6 +12,11 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
+# PyTorch first: its cuBLAS/cuDNN must be the ones the loader binds for it,
+# before anything in this process could load this repository's drop-in
+# libraries (which carry the cuBLAS 13 / cuDNN 9 sonames).
+import torch  # noqa: E402,F401
+
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs an NVIDIA B200 (sm_100a) GPU")
