@@ -120,10 +120,11 @@ fmha_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-    // heavy (late) query tiles first: blocks are dispatched in index order
-    const long long nbh = p.bh_count;
-    const int pair = p.npairs - 1 - (int)(blockIdx.x / nbh);
-    const long long bh = p.bh_begin + (long long)(blockIdx.x % nbh);
+    // the query-tile pairs of one (batch, head) are consecutive blocks, so the
+    // CTAs resident at a time share that head's K and V in L2; within a head
+    // the heavy (late, causal) pairs go first
+    const int pair = p.npairs - 1 - (int)(blockIdx.x % p.npairs);
+    const long long bh = p.bh_begin + (long long)(blockIdx.x / p.npairs);
     const int b = (int)(bh / p.heads), h = (int)(bh % p.heads);
     const int hk = h / p.kv_ratio;
     const int q0[2] = {pair * 2 * BQ, pair * 2 * BQ + BQ};

@@ -59,7 +59,14 @@ struct TcParams {
     const void* beta_dev;
 };
 
-template <int BN, int STAGES_OVERRIDE, int KIND>
+__host__ __device__ constexpr int out_es(int out) { return (out == kR16F || out == kR16BF) ? 2 : 4; }
+
+// Epilogue staging: two buffers of 32 output columns x 128 rows, laid out
+// [column][row] (rows contiguous, as in column-major C), moved to and from
+// global memory by TMA.  EPI_ES = 0: no staging (direct stores).
+constexpr int kEpiCols = 32;
+
+template <int BN, int KIND, int EPI_ES>
 struct Cfg {
     static constexpr int es = KT<KIND>::es;
     static constexpr int BK = 128 / es;          // K elements per stage (one 128-byte row)
@@ -68,11 +75,13 @@ struct Cfg {
     static constexpr int B_BYTES = BN * 128;
     static constexpr int PLANES = KT<KIND>::planes;
     static constexpr int STAGE_BYTES = (A_BYTES + B_BYTES) * PLANES;
-    static constexpr int STAGES_FIT = (kSmemBudget - kSmemReserve) / STAGE_BYTES;
-    static constexpr int STAGES = STAGES_OVERRIDE > 0 ? STAGES_OVERRIDE
-                                : (STAGES_FIT > 8 ? 8 : STAGES_FIT);
+    static constexpr int EPI_BUF = kEpiCols * BM * EPI_ES;     // one staging buffer
+    static constexpr int EPI_BYTES = 2 * EPI_BUF;
+    static constexpr int STAGES_FIT = (kSmemBudget - kSmemReserve - EPI_BYTES) / STAGE_BYTES;
+    static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
     static constexpr int TMEM_COLS = (2 * BN) < 32 ? 32 : (2 * BN);
-    static constexpr int SMEM = STAGES * STAGE_BYTES + kSmemReserve;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + EPI_BYTES + kSmemReserve;
+    static_assert(STAGES >= 2, "shared memory too small for a two-stage ring");
 };
 
 // Tile index -> (batch, tile row, tile column), walking groups of 8 tile
@@ -159,14 +168,15 @@ __device__ __forceinline__ void store_out(void* C, long long at, uint32_t raw, u
     }
 }
 
-template <int KIND, int BN, bool A_MN, bool B_MN, int OUT>
+template <int KIND, int BN, bool A_MN, bool B_MN, int OUT, bool EPI_TMA>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmA2,
                const __grid_constant__ CUtensorMap tmB2,
+               const __grid_constant__ CUtensorMap tmC,
                const TcParams p) {
-    using C_ = Cfg<BN, 0, KIND>;
+    using C_ = Cfg<BN, KIND, EPI_TMA ? out_es(OUT) : 0>;
     constexpr int BK = C_::BK, BOX = C_::BOX, STAGES = C_::STAGES;
     constexpr int A_BYTES = C_::A_BYTES, B_BYTES = C_::B_BYTES;
     constexpr int STAGE_BYTES = C_::STAGE_BYTES;
@@ -179,11 +189,13 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+    uint8_t* epi = smem + STAGES * STAGE_BYTES;            // epilogue staging buffers
+    uint64_t* full = reinterpret_cast<uint64_t*>(epi + C_::EPI_BYTES);
     uint64_t* empty = full + STAGES;
     uint64_t* tfull = empty + STAGES;
     uint64_t* tempty = tfull + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+    uint64_t* cbar = tempty + 2;                          // C chunk loaded, per buffer
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(cbar + 2);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -196,6 +208,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
         for (int a = 0; a < 2; a++) {
             mbar_init(&tfull[a], 1);
             mbar_init(&tempty[a], 4);       // one arrival per epilogue warp
+            mbar_init(&cbar[a], 1);
         }
         *abort_flag = 0;
         fence_mbar_init();
@@ -207,6 +220,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
             prefetch_tmap(&tmA2);
             prefetch_tmap(&tmB2);
         }
+        if constexpr (EPI_TMA) prefetch_tmap(&tmC);
     }
     if (warp == 1) {
         tmem_alloc(tmem_slot, TMEM_COLS);
@@ -303,54 +317,138 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
             if constexpr (OUT == kR32I) ib = *static_cast<const int32_t*>(p.beta_dev);
             else beta = *static_cast<const float*>(p.beta_dev);
         }
-        int local = 0;
-        for (int t = blockIdx.x; t < total; t += gridDim.x, local++) {
-            const int acc = local & 1;
-            const uint32_t aphase = (local >> 1) & 1;
-            if (!mbar_wait(&tfull[acc], aphase, abort_flag)) break;
-            tc_fence_after();
-            int b, tm, tn;
-            decode_tile(t, p.tiles_m, p.tiles_n, b, tm, tn);
-            const long long row = (long long)tm * BM + r_in_tile;
-            const bool row_ok = row < p.m;
-            const int n0 = tn * BN;
-            const long long base = (long long)b * p.strideC + row;
-            const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
-            const bool use_beta = OUT == kR32I ? ib != 0 : beta != 0.0f;
-            // beta * C: the old values of chunk c+1 are loaded while chunk c
-            // is converted and stored, so C's read latency is paid once per
-            // tile rather than once per column
-            uint32_t old[32], old_next[32];
-            auto fetch = [&](int c0, uint32_t (&dst)[32]) {
-#pragma unroll
-                for (int j = 0; j < 32; j++) {
-                    const int col = n0 + c0 + j;
-                    dst[j] = (use_beta && row_ok && col < p.n)
-                                 ? load_c<OUT>(p.C, base + (long long)col * p.ldc) : 0u;
-                }
-            };
-            fetch(0, old);
+        const bool use_beta = OUT == kR32I ? ib != 0 : beta != 0.0f;
+        if constexpr (EPI_TMA) {
+            // Staged epilogue.  Per 32-column chunk: the leader TMA-loads the
+            // chunk of C (for beta) into one of two staging buffers, every
+            // thread converts its row from TMEM into the buffer in place, and
+            // the leader TMA-stores the chunk (rows/columns past m/n are
+            // clipped by TMA).  The leader waits for the store that last used
+            // a buffer to finish reading it before refilling it.  Every sync
+            // point is uniform over the 128 epilogue threads: a failed bounded
+            // wait in any thread is combined with bar.red.and and all leave.
+            constexpr int ES = out_es(OUT);
+            const int et = threadIdx.x - 64;           // 0..127
+            const bool leader = et == 0;
+            uint32_t cphase = 0;                       // bit i: parity of cbar[i]
+            int chunk = 0;
+            int local = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; ok && t < total; t += gridDim.x, local++) {
+                const int acc = local & 1;
+                const uint32_t aphase = (local >> 1) & 1;
+                ok = named_bar_and(1, 128, mbar_wait(&tfull[acc], aphase, abort_flag));
+                if (!ok) break;
+                tc_fence_after();
+                int b, tm, tn;
+                decode_tile(t, p.tiles_m, p.tiles_n, b, tm, tn);
+                const int m0 = tm * BM, n0 = tn * BN;
+                const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
+                const int ncols = min(BN, p.n - n0);
 #pragma unroll 1
-            for (int c0 = 0; c0 < BN; c0 += 32) {
-                uint32_t v[32];
-                tmem_ld32(taddr + c0, v);
-                if (c0 + 32 < BN) fetch(c0 + 32, old_next);
-                tmem_wait_ld();
-                if (row_ok) {
+                for (int c0 = 0; c0 < ncols; c0 += kEpiCols, chunk++) {
+                    const int buf = chunk & 1;
+                    uint8_t* sbuf = epi + buf * C_::EPI_BUF;
+                    if (leader) {
+                        bulk_wait_read<1>();           // store of chunk-2 has read sbuf
+                        if (use_beta) {
+                            mbar_expect_tx(&cbar[buf], C_::EPI_BUF);
+                            tma_load_3d(sbuf, &tmC, &cbar[buf], m0, n0 + c0, b);
+                        }
+                    }
+                    uint32_t v[32];
+                    tmem_ld32(taddr + c0, v);
+                    bool w = true;
+                    if (use_beta) {
+                        w = mbar_wait(&cbar[buf], (cphase >> buf) & 1u, abort_flag);
+                        cphase ^= 1u << buf;
+                    }
+                    tmem_wait_ld();
+                    ok = named_bar_and(1, 128, w);
+                    if (!ok) break;
+#pragma unroll
+                    for (int j = 0; j < 32; j++) {
+                        uint8_t* e = sbuf + (j * BM + r_in_tile) * ES;
+                        if constexpr (OUT == kR32I) {
+                            uint32_t x = (uint32_t)ia * v[j];
+                            if (use_beta) x += (uint32_t)ib * *reinterpret_cast<uint32_t*>(e);
+                            *reinterpret_cast<uint32_t*>(e) = x;
+                        } else if constexpr (OUT == kR32F) {
+                            float x = alpha * __uint_as_float(v[j]);
+                            if (use_beta) x = fmaf(beta, *reinterpret_cast<float*>(e), x);
+                            *reinterpret_cast<float*>(e) = x;
+                        } else if constexpr (OUT == kR16F) {
+                            float x = alpha * __uint_as_float(v[j]);
+                            if (use_beta) x = fmaf(beta, __half2float(*reinterpret_cast<__half*>(e)), x);
+                            *reinterpret_cast<__half*>(e) = __float2half_rn(x);
+                        } else {
+                            float x = alpha * __uint_as_float(v[j]);
+                            if (use_beta)
+                                x = fmaf(beta, __bfloat162float(*reinterpret_cast<__nv_bfloat16*>(e)), x);
+                            *reinterpret_cast<__nv_bfloat16*>(e) = __float2bfloat16_rn(x);
+                        }
+                    }
+                    fence_async_smem();
+                    named_bar_sync(1, 128);
+                    if (leader) {
+                        tma_store_3d(&tmC, sbuf, m0, n0 + c0, b);
+                        bulk_commit();
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tempty[acc]);
+            }
+            if (leader) bulk_wait<0>();
+        } else {
+            int local = 0;
+            for (int t = blockIdx.x; t < total; t += gridDim.x, local++) {
+                const int acc = local & 1;
+                const uint32_t aphase = (local >> 1) & 1;
+                if (!mbar_wait(&tfull[acc], aphase, abort_flag)) break;
+                tc_fence_after();
+                int b, tm, tn;
+                decode_tile(t, p.tiles_m, p.tiles_n, b, tm, tn);
+                const long long row = (long long)tm * BM + r_in_tile;
+                const bool row_ok = row < p.m;
+                const int n0 = tn * BN;
+                const long long base = (long long)b * p.strideC + row;
+                const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
+                // beta * C: the old values of chunk c+1 are loaded while chunk c
+                // is converted and stored, so C's read latency is paid once per
+                // tile rather than once per column
+                uint32_t old[32], old_next[32];
+                auto fetch = [&](int c0, uint32_t (&dst)[32]) {
 #pragma unroll
                     for (int j = 0; j < 32; j++) {
                         const int col = n0 + c0 + j;
-                        if (col < p.n)
-                            store_out<OUT>(p.C, base + (long long)col * p.ldc, v[j], old[j],
-                                           use_beta, alpha, beta, ia, ib);
+                        dst[j] = (use_beta && row_ok && col < p.n)
+                                     ? load_c<OUT>(p.C, base + (long long)col * p.ldc) : 0u;
                     }
-                }
+                };
+                fetch(0, old);
+#pragma unroll 1
+                for (int c0 = 0; c0 < BN; c0 += 32) {
+                    uint32_t v[32];
+                    tmem_ld32(taddr + c0, v);
+                    if (c0 + 32 < BN) fetch(c0 + 32, old_next);
+                    tmem_wait_ld();
+                    if (row_ok) {
 #pragma unroll
-                for (int j = 0; j < 32; j++) old[j] = old_next[j];
+                        for (int j = 0; j < 32; j++) {
+                            const int col = n0 + c0 + j;
+                            if (col < p.n)
+                                store_out<OUT>(p.C, base + (long long)col * p.ldc, v[j], old[j],
+                                               use_beta, alpha, beta, ia, ib);
+                        }
+                    }
+#pragma unroll
+                    for (int j = 0; j < 32; j++) old[j] = old_next[j];
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tempty[acc]);
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&tempty[acc]);
         }
     }
 
@@ -421,12 +519,43 @@ bool make_tmap(CUtensorMap* tm, Kind kind, const void* base, long long inner,
     return r == CUDA_SUCCESS;
 }
 
-template <int KIND, int BN, bool A_MN, bool B_MN, int OUT>
-int launch(const GemmDesc& d, const CUtensorMap& a, const CUtensorMap& b,
-           const CUtensorMap& a2, const CUtensorMap& b2, const TcParams& p,
-           cudaStream_t s) {
-    using C_ = Cfg<BN, 0, KIND>;
-    auto kern = gemm_tc_kernel<KIND, BN, A_MN, B_MN, OUT>;
+// Tensor map of C for the staged epilogue: dims {m, n, batch}, box {128
+// rows, 32 columns, 1}, no swizzle (staging buffers are [column][row]).
+bool make_cmap(CUtensorMap* tm, const GemmDesc& d) {
+    EncodeFn enc = encode_fn();
+    if (!enc) return false;
+    CUtensorMapDataType t;
+    int es;
+    switch (d.Ctype) {
+    case kR16F: t = CU_TENSOR_MAP_DATA_TYPE_FLOAT16; es = 2; break;
+    case kR16BF: t = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16; es = 2; break;
+    case kR32F: t = CU_TENSOR_MAP_DATA_TYPE_FLOAT32; es = 4; break;
+    case kR32I: t = CU_TENSOR_MAP_DATA_TYPE_INT32; es = 4; break;
+    default: return false;
+    }
+    if ((reinterpret_cast<uintptr_t>(d.C) & 15u) || (d.ldc * es) % 16) return false;
+    if (d.batch > 1 && (d.strideC <= 0 || (d.strideC * es) % 16)) return false;
+    long long bstride = d.batch > 1 ? d.strideC : d.ldc * d.n;
+    cuuint64_t dims[3] = {(cuuint64_t)d.m, (cuuint64_t)d.n, (cuuint64_t)d.batch};
+    cuuint64_t strides[2] = {(cuuint64_t)(d.ldc * es),
+                             ((cuuint64_t)(bstride * es) + 15) & ~cuuint64_t(15)};
+    cuuint32_t box[3] = {(cuuint32_t)BM, (cuuint32_t)kEpiCols, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = enc(tm, t, 3, d.C, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+struct Maps {
+    CUtensorMap a, b, a2, b2, c;
+    bool staged;            // C described by `c`: TMA-staged epilogue
+};
+
+template <int KIND, int BN, bool A_MN, bool B_MN, int OUT, bool EPI_TMA>
+int launch_one(const Maps& m, const TcParams& p, cudaStream_t s) {
+    using C_ = Cfg<BN, KIND, EPI_TMA ? out_es(OUT) : 0>;
+    auto kern = gemm_tc_kernel<KIND, BN, A_MN, B_MN, OUT, EPI_TMA>;
     static std::atomic<unsigned long long> attr_set{0};   // one bit per device
     int dev = 0;
     cudaGetDevice(&dev);
@@ -439,45 +568,42 @@ int launch(const GemmDesc& d, const CUtensorMap& a, const CUtensorMap& b,
     }
     const int total = p.tiles_m * p.tiles_n * p.batch;
     const int grid = total < num_sms() ? total : num_sms();
-    kern<<<grid, kThreads, C_::SMEM, s>>>(a, b, a2, b2, p);
+    kern<<<grid, kThreads, C_::SMEM, s>>>(m.a, m.b, m.a2, m.b2, m.c, p);
     cudaError_t e = cudaGetLastError();
     if (e == cudaSuccess) note_launch();
     return e == cudaSuccess ? 0 : (int)e;
 }
 
-template <int KIND, int BN, bool A_MN, bool B_MN>
-int launch_out(const GemmDesc& d, const CUtensorMap& a, const CUtensorMap& b,
-               const CUtensorMap& a2, const CUtensorMap& b2, const TcParams& p,
-               cudaStream_t s) {
-    switch (d.Ctype) {
-    case kR16F: return launch<KIND, BN, A_MN, B_MN, kR16F>(d, a, b, a2, b2, p, s);
-    case kR16BF: return launch<KIND, BN, A_MN, B_MN, kR16BF>(d, a, b, a2, b2, p, s);
-    case kR32F: return launch<KIND, BN, A_MN, B_MN, kR32F>(d, a, b, a2, b2, p, s);
-    default: return 1;
-    }
+template <int KIND, int BN, bool A_MN, bool B_MN, int OUT>
+int launch(const Maps& m, const TcParams& p, cudaStream_t s) {
+    return m.staged ? launch_one<KIND, BN, A_MN, B_MN, OUT, true>(m, p, s)
+                    : launch_one<KIND, BN, A_MN, B_MN, OUT, false>(m, p, s);
+}
+
+template <int KIND, int BN, int OUT>
+int launch_majors(bool a_mn, bool b_mn, const Maps& m, const TcParams& p, cudaStream_t s) {
+    if (a_mn && b_mn) return launch<KIND, BN, true, true, OUT>(m, p, s);
+    if (a_mn) return launch<KIND, BN, true, false, OUT>(m, p, s);
+    if (b_mn) return launch<KIND, BN, false, true, OUT>(m, p, s);
+    return launch<KIND, BN, false, false, OUT>(m, p, s);
 }
 
 template <int KIND, int BN>
-int launch_major(const GemmDesc& d, bool a_mn, bool b_mn, const CUtensorMap& a,
-                 const CUtensorMap& b, const CUtensorMap& a2, const CUtensorMap& b2,
-                 const TcParams& p, cudaStream_t s) {
+int launch_major(const GemmDesc& d, bool a_mn, bool b_mn, const Maps& m, const TcParams& p,
+                 cudaStream_t s) {
     if constexpr (KIND == (int)Kind::I8) {
         if (d.Ctype != kR32I) return 1;
-        if (a_mn && b_mn) return launch<KIND, BN, true, true, kR32I>(d, a, b, a2, b2, p, s);
-        if (a_mn) return launch<KIND, BN, true, false, kR32I>(d, a, b, a2, b2, p, s);
-        if (b_mn) return launch<KIND, BN, false, true, kR32I>(d, a, b, a2, b2, p, s);
-        return launch<KIND, BN, false, false, kR32I>(d, a, b, a2, b2, p, s);
+        return launch_majors<KIND, BN, kR32I>(a_mn, b_mn, m, p, s);
     } else if constexpr (KIND == (int)Kind::TF32X3 || KIND == (int)Kind::TF32) {
         if (d.Ctype != kR32F) return 1;
-        if (a_mn && b_mn) return launch<KIND, BN, true, true, kR32F>(d, a, b, a2, b2, p, s);
-        if (a_mn) return launch<KIND, BN, true, false, kR32F>(d, a, b, a2, b2, p, s);
-        if (b_mn) return launch<KIND, BN, false, true, kR32F>(d, a, b, a2, b2, p, s);
-        return launch<KIND, BN, false, false, kR32F>(d, a, b, a2, b2, p, s);
+        return launch_majors<KIND, BN, kR32F>(a_mn, b_mn, m, p, s);
     } else {
-        if (a_mn && b_mn) return launch_out<KIND, BN, true, true>(d, a, b, a2, b2, p, s);
-        if (a_mn) return launch_out<KIND, BN, true, false>(d, a, b, a2, b2, p, s);
-        if (b_mn) return launch_out<KIND, BN, false, true>(d, a, b, a2, b2, p, s);
-        return launch_out<KIND, BN, false, false>(d, a, b, a2, b2, p, s);
+        switch (d.Ctype) {
+        case kR16F: return launch_majors<KIND, BN, kR16F>(a_mn, b_mn, m, p, s);
+        case kR16BF: return launch_majors<KIND, BN, kR16BF>(a_mn, b_mn, m, p, s);
+        case kR32F: return launch_majors<KIND, BN, kR32F>(a_mn, b_mn, m, p, s);
+        default: return 1;
+        }
     }
 }
 
@@ -528,7 +654,8 @@ int gemm_tc(const GemmDesc& d, cudaStream_t s) {
         if (tiles128 < sms) BN = 64;
     }
 
-    CUtensorMap ta, tb, ta2, tb2;
+    Maps maps;
+    CUtensorMap &ta = maps.a, &tb = maps.b, &ta2 = maps.a2, &tb2 = maps.b2;
     auto mk = [&](CUtensorMap* tm, const void* base, bool mn, long long mn_ext, long long ld,
                   long long stride, int rows) {
         if (mn) return make_tmap(tm, d.kind, base, mn_ext, d.k, ld, stride, d.batch, box, bk);
@@ -543,6 +670,8 @@ int gemm_tc(const GemmDesc& d, cudaStream_t s) {
         ta2 = ta;
         tb2 = tb;
     }
+    maps.staged = !getenv("ZBLAS_NO_TMA_EPILOGUE") && make_cmap(&maps.c, d);
+    if (!maps.staged) maps.c = ta;
 
     TcParams p;
     p.m = d.m; p.n = d.n; p.k = d.k; p.batch = d.batch;
@@ -559,20 +688,20 @@ int gemm_tc(const GemmDesc& d, cudaStream_t s) {
 
     switch (d.kind) {
     case Kind::F16:
-        return BN == 256 ? launch_major<(int)Kind::F16, 256>(d, a_mn, b_mn, ta, tb, ta2, tb2, p, s)
-                         : launch_major<(int)Kind::F16, 128>(d, a_mn, b_mn, ta, tb, ta2, tb2, p, s);
+        return BN == 256 ? launch_major<(int)Kind::F16, 256>(d, a_mn, b_mn, maps, p, s)
+                         : launch_major<(int)Kind::F16, 128>(d, a_mn, b_mn, maps, p, s);
     case Kind::BF16:
-        return BN == 256 ? launch_major<(int)Kind::BF16, 256>(d, a_mn, b_mn, ta, tb, ta2, tb2, p, s)
-                         : launch_major<(int)Kind::BF16, 128>(d, a_mn, b_mn, ta, tb, ta2, tb2, p, s);
+        return BN == 256 ? launch_major<(int)Kind::BF16, 256>(d, a_mn, b_mn, maps, p, s)
+                         : launch_major<(int)Kind::BF16, 128>(d, a_mn, b_mn, maps, p, s);
     case Kind::I8:
-        return BN == 256 ? launch_major<(int)Kind::I8, 256>(d, a_mn, b_mn, ta, tb, ta2, tb2, p, s)
-                         : launch_major<(int)Kind::I8, 128>(d, a_mn, b_mn, ta, tb, ta2, tb2, p, s);
+        return BN == 256 ? launch_major<(int)Kind::I8, 256>(d, a_mn, b_mn, maps, p, s)
+                         : launch_major<(int)Kind::I8, 128>(d, a_mn, b_mn, maps, p, s);
     case Kind::TF32:
-        return BN == 256 ? launch_major<(int)Kind::TF32, 256>(d, a_mn, b_mn, ta, tb, ta2, tb2, p, s)
-                         : launch_major<(int)Kind::TF32, 128>(d, a_mn, b_mn, ta, tb, ta2, tb2, p, s);
+        return BN == 256 ? launch_major<(int)Kind::TF32, 256>(d, a_mn, b_mn, maps, p, s)
+                         : launch_major<(int)Kind::TF32, 128>(d, a_mn, b_mn, maps, p, s);
     case Kind::TF32X3:
-        return BN == 128 ? launch_major<(int)Kind::TF32X3, 128>(d, a_mn, b_mn, ta, tb, ta2, tb2, p, s)
-                         : launch_major<(int)Kind::TF32X3, 64>(d, a_mn, b_mn, ta, tb, ta2, tb2, p, s);
+        return BN == 128 ? launch_major<(int)Kind::TF32X3, 128>(d, a_mn, b_mn, maps, p, s)
+                         : launch_major<(int)Kind::TF32X3, 64>(d, a_mn, b_mn, maps, p, s);
     }
     return 1;
 }

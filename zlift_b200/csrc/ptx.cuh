@@ -137,6 +137,50 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* m,
         : "memory");
 }
 
+// shared -> global tiled store (bulk async group); out-of-range elements of
+// the box are not written
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* m, const void* src, int x,
+                                             int y, int z) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];"
+        :: "l"(reinterpret_cast<uint64_t>(m)), "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
+        : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() {
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+// wait until at most N committed bulk groups still read shared memory
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" :: "n"(N) : "memory");
+}
+
+// wait until at most N committed bulk groups are incomplete (writes done)
+template <int N>
+__device__ __forceinline__ void bulk_wait() {
+    asm volatile("cp.async.bulk.wait_group %0;" :: "n"(N) : "memory");
+}
+
+// barrier among `count` threads (a multiple of 32) on hardware barrier `id`
+__device__ __forceinline__ void named_bar_sync(int id, int count) {
+    asm volatile("bar.sync %0, %1;" :: "r"(id), "r"(count) : "memory");
+}
+
+// the same barrier, returning the AND of every participant's `pred`: lets a
+// group leave a loop together when any member's bounded wait failed
+__device__ __forceinline__ bool named_bar_and(int id, int count, bool pred) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.and.pred q, %2, %3, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r) : "r"((uint32_t)pred), "r"(id), "r"(count) : "memory");
+    return r != 0;
+}
+
 // ---- tcgen05 --------------------------------------------------------------
 
 // Allocate `ncols` TMEM columns (power of two, >= 32); one full warp calls
