@@ -253,3 +253,35 @@ def test_sgemm_tf32_math_mode(handle, oracle_lib):
         assert err < 5e-3
     finally:
         handle.set_math_mode(blas.DEFAULT_MATH)
+
+
+# Shapes large enough for the CTA-pair kernel (256-row tiles split over two
+# SMs): >= 148 tiles of 128 x 256 and >= 74 pair tiles.  M = 1200 leaves the
+# second CTA of the last pair tile partly past the end of C.
+@pytest.mark.parametrize("kind", ["f16", "bf16", "i8"])
+@pytest.mark.parametrize("ta,tb", [(0, 1), (1, 0), (0, 0), (1, 1)])
+def test_pair_tiles(handle, oracle_lib, kind, ta, tb):
+    if kind == "i8":
+        run_gemm(handle, oracle_lib, "i8", "i32", ta, tb, 1200, 4000, 2080, 2, -1, dist="int8")
+    else:
+        run_gemm(handle, oracle_lib, kind, kind, ta, tb, 1200, 4000, 1040, 1.0, 0.5, seed=7)
+
+
+def test_pair_tiles_f32_out(handle, oracle_lib):
+    run_gemm(handle, oracle_lib, "bf16", "f32", 0, 1, 2048, 2560, 1024, 0.5, 0.0, seed=3)
+
+
+def test_pair_tiles_strided_batched(handle, oracle_lib):
+    from zlift_b200 import inputs
+    m, n, k, batch = 256, 256, 1024, 150
+    A = inputs.make("bf16", "normal", 21, m * k * batch)
+    B = inputs.make("bf16", "normal", 22, k * n * batch)
+    C0 = np.zeros(m * n * batch, np.uint16)
+    cref = C0.copy()
+    assert oracle_lib.gemm_strided_batched_ex(0, 0, m, n, k, 0.125, A, 14, m, m * k, B, 14, k,
+                                              k * n, 0.0, cref, 14, m, m * n, batch) == 0
+    dA, dB, dC = to_dev(A, "bf16"), to_dev(B, "bf16"), to_dev(C0, "bf16")
+    assert handle.gemm_strided_batched_ex(0, 0, m, n, k, 0.125, dA, 14, m, m * k, dB, 14, k,
+                                          k * n, 0.0, dC, 14, m, m * n, batch) == 0
+    got = as_float(from_dev(dC, "bf16"), "bf16")
+    assert normwise(got, as_float(cref, "bf16")) <= 1e-2

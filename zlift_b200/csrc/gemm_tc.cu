@@ -66,13 +66,15 @@ __host__ __device__ constexpr int out_es(int out) { return (out == kR16F || out 
 // global memory by TMA.  EPI_ES = 0: no staging (direct stores).
 constexpr int kEpiCols = 32;
 
-template <int BN, int KIND, int EPI_ES>
+template <int BN, int KIND, int EPI_ES, bool PAIR = false>
 struct Cfg {
     static constexpr int es = KT<KIND>::es;
     static constexpr int BK = 128 / es;          // K elements per stage (one 128-byte row)
     static constexpr int BOX = 128 / es;         // MN elements in one 128-byte row
     static constexpr int A_BYTES = BM * 128;
-    static constexpr int B_BYTES = BN * 128;
+    // a CTA pair splits B's BN columns: each CTA holds BN/2 of them
+    static constexpr int B_ROWS = PAIR ? BN / 2 : BN;
+    static constexpr int B_BYTES = B_ROWS * 128;
     static constexpr int PLANES = KT<KIND>::planes;
     static constexpr int STAGE_BYTES = (A_BYTES + B_BYTES) * PLANES;
     static constexpr int EPI_BUF = kEpiCols * BM * EPI_ES;     // one staging buffer
@@ -118,6 +120,27 @@ __device__ __forceinline__ void load_operand(uint8_t* dst, const CUtensorMap* tm
         for (int i = 0; i < ROWS / BOX; i++)
             tma_load_3d(dst + i * (BK * 128), tm, bar, mn0 + i * BOX, k0, b);
     }
+}
+
+// Pair form: completion bytes go to the leader CTA's barrier `bar0`
+// (shared::cluster address).
+template <bool MN, int ROWS, int BK, int BOX>
+__device__ __forceinline__ void load_operand_pair(uint8_t* dst, const CUtensorMap* tm,
+                                                  uint32_t bar0, int mn0, int k0, int b) {
+    if constexpr (!MN) {
+        tma_load_3d_pair(dst, tm, bar0, k0, mn0, b);
+    } else {
+#pragma unroll
+        for (int i = 0; i < ROWS / BOX; i++)
+            tma_load_3d_pair(dst + i * (BK * 128), tm, bar0, mn0 + i * BOX, k0, b);
+    }
+}
+
+// An epilogue warp is done with an accumulator: arrive on the MMA issuer's
+// barrier (the leader CTA's, for a pair).
+__device__ __forceinline__ void release_acc(uint64_t* bar, uint32_t rank) {
+    if (rank == 0) mbar_arrive(bar);
+    else mbar_arrive_cluster(mapa_shared(bar, 0));
 }
 
 // Descriptor of K step `ks` (uk elements of K) of an operand tile.
@@ -168,7 +191,7 @@ __device__ __forceinline__ void store_out(void* C, long long at, uint32_t raw, u
     }
 }
 
-template <int KIND, int BN, bool A_MN, bool B_MN, int OUT, bool EPI_TMA>
+template <int KIND, int BN, bool A_MN, bool B_MN, int OUT, bool EPI_TMA, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                const __grid_constant__ CUtensorMap tmB,
@@ -176,14 +199,16 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                const __grid_constant__ CUtensorMap tmB2,
                const __grid_constant__ CUtensorMap tmC,
                const TcParams p) {
-    using C_ = Cfg<BN, KIND, EPI_TMA ? out_es(OUT) : 0>;
+    using C_ = Cfg<BN, KIND, EPI_TMA ? out_es(OUT) : 0, PAIR>;
     constexpr int BK = C_::BK, BOX = C_::BOX, STAGES = C_::STAGES;
+    constexpr int B_ROWS = C_::B_ROWS;
+    constexpr int TILE_M = PAIR ? 2 * BM : BM;           // output rows per tile
     constexpr int A_BYTES = C_::A_BYTES, B_BYTES = C_::B_BYTES;
     constexpr int STAGE_BYTES = C_::STAGE_BYTES;
     constexpr int UK = KT<KIND>::uk;
     constexpr int KSTEPS = BK / UK;
     constexpr uint32_t IDESC =
-        make_idesc(KT<KIND>::cfmt, KT<KIND>::abfmt, A_MN ? 1 : 0, B_MN ? 1 : 0, BM, BN);
+        make_idesc(KT<KIND>::cfmt, KT<KIND>::abfmt, A_MN ? 1 : 0, B_MN ? 1 : 0, TILE_M, BN);
     constexpr uint32_t TMEM_COLS = C_::TMEM_COLS;
 
     extern __shared__ uint8_t smem_raw[];
@@ -199,6 +224,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // CTA pair: rank 0 (leader) issues the MMAs for both; each CTA loads its
+    // own 128 rows of A and BN/2 columns of B and stores its 128 rows of C
+    const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+    const int cta_id = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+    const int n_ctas = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) {
@@ -207,7 +237,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
         }
         for (int a = 0; a < 2; a++) {
             mbar_init(&tfull[a], 1);
-            mbar_init(&tempty[a], 4);       // one arrival per epilogue warp
+            mbar_init(&tempty[a], PAIR ? 8 : 4);   // one arrival per epilogue warp (of both CTAs)
             mbar_init(&cbar[a], 1);
         }
         *abort_flag = 0;
@@ -223,11 +253,17 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
         if constexpr (EPI_TMA) prefetch_tmap(&tmC);
     }
     if (warp == 1) {
-        tmem_alloc(tmem_slot, TMEM_COLS);
-        tmem_relinquish();
+        if constexpr (PAIR) {
+            tmem_alloc_pair(tmem_slot, TMEM_COLS);
+            tmem_relinquish_pair();
+        } else {
+            tmem_alloc(tmem_slot, TMEM_COLS);
+            tmem_relinquish();
+        }
     }
     tc_fence_before();
-    __syncthreads();
+    if constexpr (PAIR) cluster_sync();    // barriers of both CTAs initialised
+    else __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
@@ -238,16 +274,26 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
         if (lane == 0) {
             int stage = 0;
             uint32_t phase = 0;
-            for (int t = blockIdx.x; t < total; t += gridDim.x) {
+            for (int t = cta_id; t < total; t += n_ctas) {
                 int b, tm, tn;
                 decode_tile(t, p.tiles_m, p.tiles_n, b, tm, tn);
-                const int m0 = tm * BM, n0 = tn * BN;
+                const int m0 = tm * TILE_M + (int)rank * BM;
+                const int n0 = tn * BN + (int)rank * B_ROWS;
                 for (int kb = 0; kb < p.k_blocks; kb++) {
                     if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) goto producer_done;
                     uint8_t* sa = smem + stage * STAGE_BYTES;
                     uint8_t* sb = sa + A_BYTES;
-                    mbar_expect_tx(&full[stage], STAGE_BYTES);
                     const int k0 = kb * BK;
+                    if constexpr (PAIR) {
+                        // both CTAs' bytes complete on the leader's barrier
+                        if (rank == 0) mbar_expect_tx(&full[stage], 2 * STAGE_BYTES);
+                        const uint32_t bar0 = mapa_shared(&full[stage], 0);
+                        load_operand_pair<A_MN, BM, BK, BOX>(sa, &tmA, bar0, m0, k0, b);
+                        load_operand_pair<B_MN, B_ROWS, BK, BOX>(sb, &tmB, bar0, n0, k0, b);
+                        if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+                        continue;
+                    }
+                    mbar_expect_tx(&full[stage], STAGE_BYTES);
                     load_operand<A_MN, BM, BK, BOX>(sa, &tmA, &full[stage], m0, k0, b);
                     load_operand<B_MN, BN, BK, BOX>(sb, &tmB, &full[stage], n0, k0, b);
                     if constexpr (C_::PLANES == 2) {
@@ -257,15 +303,22 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                     if (++stage == STAGES) { stage = 0; phase ^= 1u; }
                 }
             }
+            // drain: wait until the MMA issuer has released every stage, so no
+            // tcgen05.commit arrival is still travelling to this CTA's barriers
+            // when it exits (for a pair they come from the other SM)
+            for (int i = 0; i < STAGES; i++) {
+                if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) break;
+                if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+            }
         producer_done:;
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
-        if (lane == 0) {
+        if (lane == 0 && rank == 0) {
             int stage = 0;
             uint32_t phase = 0;
             int local = 0;
-            for (int t = blockIdx.x; t < total; t += gridDim.x, local++) {
+            for (int t = cta_id; t < total; t += n_ctas, local++) {
                 const int acc = local & 1;
                 const uint32_t aphase = (local >> 1) & 1;
                 if (!mbar_wait(&tempty[acc], aphase ^ 1u, abort_flag)) break;
@@ -291,15 +344,19 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                         } else if constexpr (KIND == (int)Kind::TF32) {
                             mma_tf32_ss(d, ad, bd, IDESC, accum);
                         } else if constexpr (KIND == (int)Kind::I8) {
-                            mma_i8_ss(d, ad, bd, IDESC, accum);
+                            if constexpr (PAIR) mma_i8_ss_pair(d, ad, bd, IDESC, accum);
+                            else mma_i8_ss(d, ad, bd, IDESC, accum);
                         } else {
-                            mma_f16_ss(d, ad, bd, IDESC, accum);
+                            if constexpr (PAIR) mma_f16_ss_pair(d, ad, bd, IDESC, accum);
+                            else mma_f16_ss(d, ad, bd, IDESC, accum);
                         }
                     }
-                    mma_commit(&empty[stage]);
+                    if constexpr (PAIR) mma_commit_pair(&empty[stage], 0x3);
+                    else mma_commit(&empty[stage]);
                     if (++stage == STAGES) { stage = 0; phase ^= 1u; }
                 }
-                mma_commit(&tfull[acc]);
+                if constexpr (PAIR) mma_commit_pair(&tfull[acc], 0x3);
+                else mma_commit(&tfull[acc]);
             }
         mma_done:;
         }
@@ -334,7 +391,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
             int chunk = 0;
             int local = 0;
             bool ok = true;
-            for (int t = blockIdx.x; ok && t < total; t += gridDim.x, local++) {
+            for (int t = cta_id; ok && t < total; t += n_ctas, local++) {
                 const int acc = local & 1;
                 const uint32_t aphase = (local >> 1) & 1;
                 ok = named_bar_and(1, 128, mbar_wait(&tfull[acc], aphase, abort_flag));
@@ -342,7 +399,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                 tc_fence_after();
                 int b, tm, tn;
                 decode_tile(t, p.tiles_m, p.tiles_n, b, tm, tn);
-                const int m0 = tm * BM, n0 = tn * BN;
+                const int m0 = tm * TILE_M + (int)rank * BM, n0 = tn * BN;
                 const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
                 const int ncols = min(BN, p.n - n0);
 #pragma unroll 1
@@ -397,19 +454,19 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                 }
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&tempty[acc]);
+                if (lane == 0) release_acc(&tempty[acc], rank);
             }
             if (leader) bulk_wait<0>();
         } else {
             int local = 0;
-            for (int t = blockIdx.x; t < total; t += gridDim.x, local++) {
+            for (int t = cta_id; t < total; t += n_ctas, local++) {
                 const int acc = local & 1;
                 const uint32_t aphase = (local >> 1) & 1;
                 if (!mbar_wait(&tfull[acc], aphase, abort_flag)) break;
                 tc_fence_after();
                 int b, tm, tn;
                 decode_tile(t, p.tiles_m, p.tiles_n, b, tm, tn);
-                const long long row = (long long)tm * BM + r_in_tile;
+                const long long row = (long long)tm * TILE_M + (int)rank * BM + r_in_tile;
                 const bool row_ok = row < p.m;
                 const int n0 = tn * BN;
                 const long long base = (long long)b * p.strideC + row;
@@ -447,15 +504,18 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                 }
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&tempty[acc]);
+                if (lane == 0) release_acc(&tempty[acc], rank);
             }
         }
     }
 
-    __syncthreads();
+    tc_fence_before();
+    if constexpr (PAIR) cluster_sync();   // neither CTA leaves while its pair may signal it
+    else __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem_base, TMEM_COLS);
+        if constexpr (PAIR) tmem_dealloc_pair(tmem_base, TMEM_COLS);
+        else tmem_dealloc(tmem_base, TMEM_COLS);
     }
 }
 
@@ -550,13 +610,21 @@ bool make_cmap(CUtensorMap* tm, const GemmDesc& d) {
 struct Maps {
     CUtensorMap a, b, a2, b2, c;
     bool staged;            // C described by `c`: TMA-staged epilogue
+    bool pair;              // CTA-pair (cta_group::2) kernel, 256-row tiles
 };
 
-template <int KIND, int BN, bool A_MN, bool B_MN, int OUT, bool EPI_TMA>
+// Kinds and widths the CTA-pair kernel is built for.
+constexpr bool pair_ok(int kind, int bn) {
+    return bn == 256 && (kind == (int)Kind::F16 || kind == (int)Kind::BF16 ||
+                         kind == (int)Kind::I8);
+}
+
+template <int KIND, int BN, bool A_MN, bool B_MN, int OUT, bool EPI_TMA, bool PAIR>
 int launch_one(const Maps& m, const TcParams& p, cudaStream_t s) {
-    using C_ = Cfg<BN, KIND, EPI_TMA ? out_es(OUT) : 0>;
-    auto kern = gemm_tc_kernel<KIND, BN, A_MN, B_MN, OUT, EPI_TMA>;
+    using C_ = Cfg<BN, KIND, EPI_TMA ? out_es(OUT) : 0, PAIR>;
+    auto kern = gemm_tc_kernel<KIND, BN, A_MN, B_MN, OUT, EPI_TMA, PAIR>;
     static std::atomic<unsigned long long> attr_set{0};   // one bit per device
+    static int max_clusters[64] = {0};                    // co-resident pairs per device
     int dev = 0;
     cudaGetDevice(&dev);
     const unsigned long long bit = 1ull << (dev & 63);
@@ -564,20 +632,65 @@ int launch_one(const Maps& m, const TcParams& p, cudaStream_t s) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              C_::SMEM);
         if (e != cudaSuccess) return (int)e;
+        if constexpr (PAIR) {
+            e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
+            cudaLaunchConfig_t q = {};
+            q.gridDim = dim3(2 * (num_sms() / 2));
+            q.blockDim = dim3(kThreads);
+            q.dynamicSmemBytes = C_::SMEM;
+            cudaLaunchAttribute qa[1];
+            qa[0].id = cudaLaunchAttributeClusterDimension;
+            qa[0].val.clusterDim.x = 2;
+            qa[0].val.clusterDim.y = 1;
+            qa[0].val.clusterDim.z = 1;
+            q.attrs = qa;
+            q.numAttrs = 1;
+            int nc = 0;
+            e = cudaOccupancyMaxActiveClusters(&nc, kern, &q);
+            if (e != cudaSuccess || nc <= 0) {
+                cudaGetLastError();
+                nc = num_sms() / 2;
+            }
+            max_clusters[dev & 63] = nc;
+        }
         attr_set.fetch_or(bit);
     }
     const int total = p.tiles_m * p.tiles_n * p.batch;
-    const int grid = total < num_sms() ? total : num_sms();
-    kern<<<grid, kThreads, C_::SMEM, s>>>(m.a, m.b, m.a2, m.b2, m.c, p);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e;
+    if constexpr (PAIR) {
+        const int slots = max_clusters[dev & 63] > 0 ? max_clusters[dev & 63] : num_sms() / 2;
+        const int clusters = total < slots ? total : slots;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2 * clusters);
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = C_::SMEM;
+        cfg.stream = s;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        e = cudaLaunchKernelEx(&cfg, kern, m.a, m.b, m.a2, m.b2, m.c, p);
+    } else {
+        const int grid = total < num_sms() ? total : num_sms();
+        kern<<<grid, kThreads, C_::SMEM, s>>>(m.a, m.b, m.a2, m.b2, m.c, p);
+        e = cudaGetLastError();
+    }
     if (e == cudaSuccess) note_launch();
     return e == cudaSuccess ? 0 : (int)e;
 }
 
 template <int KIND, int BN, bool A_MN, bool B_MN, int OUT>
 int launch(const Maps& m, const TcParams& p, cudaStream_t s) {
-    return m.staged ? launch_one<KIND, BN, A_MN, B_MN, OUT, true>(m, p, s)
-                    : launch_one<KIND, BN, A_MN, B_MN, OUT, false>(m, p, s);
+    if constexpr (pair_ok(KIND, BN)) {
+        if (m.pair)
+            return m.staged ? launch_one<KIND, BN, A_MN, B_MN, OUT, true, true>(m, p, s)
+                            : launch_one<KIND, BN, A_MN, B_MN, OUT, false, true>(m, p, s);
+    }
+    return m.staged ? launch_one<KIND, BN, A_MN, B_MN, OUT, true, false>(m, p, s)
+                    : launch_one<KIND, BN, A_MN, B_MN, OUT, false, false>(m, p, s);
 }
 
 template <int KIND, int BN, int OUT>
@@ -655,6 +768,14 @@ int gemm_tc(const GemmDesc& d, cudaStream_t s) {
     }
 
     Maps maps;
+    // CTA pairs (256-row tiles, B split between the two SMs) when there are
+    // enough pair tiles to occupy the GPU
+    const long long pair_tiles =
+        (long long)((d.m + 2 * BM - 1) / (2 * BM)) * ((d.n + BN - 1) / BN) * d.batch;
+    // (short K: the pair's extra synchronisation outweighs the halved B loads)
+    maps.pair = pair_ok((int)d.kind, BN) && !getenv("ZBLAS_NO_PAIR") && pair_tiles >= sms / 2 &&
+                (long long)d.k * es >= 2048;
+    const int b_rows = maps.pair ? BN / 2 : BN;
     CUtensorMap &ta = maps.a, &tb = maps.b, &ta2 = maps.a2, &tb2 = maps.b2;
     auto mk = [&](CUtensorMap* tm, const void* base, bool mn, long long mn_ext, long long ld,
                   long long stride, int rows) {
@@ -662,7 +783,7 @@ int gemm_tc(const GemmDesc& d, cudaStream_t s) {
         return make_tmap(tm, d.kind, base, d.k, mn_ext, ld, stride, d.batch, bk, rows);
     };
     if (!mk(&ta, a_base, a_mn, d.m, d.lda, d.strideA, BM)) return 1;
-    if (!mk(&tb, b_base, b_mn, d.n, d.ldb, d.strideB, BN)) return 1;
+    if (!mk(&tb, b_base, b_mn, d.n, d.ldb, d.strideB, b_rows)) return 1;
     if (d.kind == Kind::TF32X3) {
         if (!mk(&ta2, d.A_lo, a_mn, d.m, d.lda, d.strideA, BM)) return 1;
         if (!mk(&tb2, d.B_lo, b_mn, d.n, d.ldb, d.strideB, BN)) return 1;
@@ -675,7 +796,7 @@ int gemm_tc(const GemmDesc& d, cudaStream_t s) {
 
     TcParams p;
     p.m = d.m; p.n = d.n; p.k = d.k; p.batch = d.batch;
-    p.tiles_m = (d.m + BM - 1) / BM;
+    p.tiles_m = maps.pair ? (d.m + 2 * BM - 1) / (2 * BM) : (d.m + BM - 1) / BM;
     p.tiles_n = (d.n + BN - 1) / BN;
     p.k_blocks = (d.k + bk - 1) / bk;
     p.ldc = d.ldc;
