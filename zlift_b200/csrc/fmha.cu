@@ -31,6 +31,7 @@
 
 #include <atomic>
 #include <cmath>
+#include <cstdlib>
 
 namespace zl {
 
@@ -72,6 +73,27 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
+// 2^x on the FMA/ALU pipes, for a share of the softmax exponentials so that
+// the MUFU unit (16 exp2 per clock per SM, as busy as the tensor core at
+// head_dim 128) is not the bottleneck.  Cody-Waite range reduction:
+// x = j + f with j = round(x) (obtained by adding 1.5 * 2^23, which leaves j
+// in the low mantissa bits) and f in [-1/2, 1/2]; 2^f from a degree-3
+// polynomial of least maximum relative error (Remez exchange, 7.5e-5; see
+// fit_exp2_poly.py); 2^j applied by adding j to the exponent field.
+// Arguments below -126 (masked scores are -inf) give exactly 0.
+__device__ __forceinline__ float ex2_poly(float x) {
+    constexpr float kC0 = 0.9999280571937561f, kC1 = 0.6932609677314758f,
+                    kC2 = 0.2426111251115799f, kC3 = 0.0551716685295105f;
+    constexpr float kShift = 12582912.0f;       // 1.5 * 2^23
+    const float xc = fmaxf(x, -126.0f);
+    const float t = xc + kShift;
+    const float f = xc - (t - kShift);
+    const int j = __float_as_int(t) - 0x4B400000;
+    const float p = fmaf(fmaf(fmaf(kC3, f, kC2), f, kC1), f, kC0);
+    const float y = __int_as_float(__float_as_int(p) + (j << 23));
+    return x < -126.0f ? 0.0f : y;
+}
+
 template <bool BF16>
 __device__ __forceinline__ uint32_t pack2(float a, float b) {
     if constexpr (BF16) {
@@ -93,7 +115,9 @@ __device__ __forceinline__ int key_tiles(const FParams& p, int q0) {
     return min(last_key / BKEY + 1, p.nkt);
 }
 
-template <int D, bool BF16>
+// POLY: 0 = every exponential on MUFU; k > 0 = one column pair in k by
+// ex2_poly on the FMA pipe.
+template <int D, bool BF16, int POLY>
 __global__ void __launch_bounds__(kThreads, 1)
 fmha_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
                 const __grid_constant__ CUtensorMap tmK,
@@ -115,7 +139,8 @@ fmha_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
     uint64_t* sfull = bars + 7;       // [2] per query tile
     uint64_t* pready = bars + 9;      // [2]
     uint64_t* ofinal = bars + 11;     // [2]
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
+    uint64_t* phalf = bars + 13;      // [2] first half of P (keys 0-63) stored
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -127,9 +152,11 @@ fmha_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
     const long long bh = p.bh_begin + (long long)(blockIdx.x / p.npairs);
     const int b = (int)(bh / p.heads), h = (int)(bh % p.heads);
     const int hk = h / p.kv_ratio;
-    const int q0[2] = {pair * 2 * BQ, pair * 2 * BQ + BQ};
-    const int nt[2] = {key_tiles(p, q0[0]), key_tiles(p, q0[1])};
-    const int nmax = max(nt[0], nt[1]);
+    // (scalars, not arrays: the warps index them by tile and an indexed array
+    // would live in local memory)
+    const int q00 = pair * 2 * BQ, q01 = q00 + BQ;
+    const int nt0 = key_tiles(p, q00), nt1 = key_tiles(p, q01);
+    const int nmax = max(nt0, nt1);
 
     if (threadIdx.x == 0) {
         mbar_init(qfull, 1);
@@ -139,6 +166,7 @@ fmha_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
             mbar_init(&kvempty[i], 1);
             mbar_init(&sfull[i], 1);
             mbar_init(&pready[i], 4);
+            mbar_init(&phalf[i], 4);
             mbar_init(&ofinal[i], 1);
         }
         *abort_flag = 0;
@@ -163,7 +191,7 @@ fmha_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
             for (int t = 0; t < 2; t++)
                 for (int x = 0; x < C::BOXES; x++)
                     tma_load_4d(smem + C::Q_OFF + t * C::TILE_BYTES + x * BOX_BYTES, &tmQ, qfull,
-                                x * 64, q0[t], h, b);
+                                x * 64, t ? q01 : q00, h, b);
             for (int j = 0; j < nmax; j++) {
                 const int st = j & 1;
                 if (!mbar_wait(&kvempty[st], ((j >> 1) & 1) ^ 1u, abort_flag)) break;
@@ -194,11 +222,12 @@ fmha_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
                 }
                 mma_commit(&sfull[t]);
             };
-            auto issue_pv = [&](int t, int j) {
+            // half 0: keys 0-63 of the tile, half 1: keys 64-127
+            auto issue_pv = [&](int t, int j, int half) {
                 const uint32_t vb =
                     smem_u32(smem + C::KV_OFF + (j & 1) * 2 * C::TILE_BYTES + C::TILE_BYTES);
 #pragma unroll
-                for (int ks = 0; ks < BKEY / 16; ks++) {
+                for (int ks = half * (BKEY / 32); ks < (half + 1) * (BKEY / 32); ks++) {
                     // P: 16 keys = 8 packed TMEM columns per step; V: 16 key rows
                     mma_f16_ts(tmem_base + ocol[t], tmem_base + scol[t] + ks * 8,
                                sw128_desc(vb + ks * 16 * 128, BOX_BYTES, 1024), IDESC_PV,
@@ -208,8 +237,8 @@ fmha_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
             bool ok = mbar_wait(qfull, 0, abort_flag) && mbar_wait(&kfull[0], 0, abort_flag);
             if (ok) {
                 tc_fence_after();
-                for (int t = 0; t < 2; t++)
-                    if (nt[t] > 0) issue_qk(t, 0);
+                if (nt0 > 0) issue_qk(0, 0);
+                if (nt1 > 0) issue_qk(1, 0);
             }
             for (int j = 0; ok && j < nmax; j++) {
                 const int st = j & 1;
@@ -217,13 +246,19 @@ fmha_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
                 if (!mbar_wait(&vfull[st], kv_par, abort_flag)) break;
                 const bool next_k = j + 1 < nmax;
                 bool have_next_k = false;
+#pragma unroll
                 for (int t = 0; t < 2; t++) {
-                    if (j >= nt[t]) continue;
+                    const int ntt = t ? nt1 : nt0;
+                    if (j >= ntt) continue;
+                    // P.V on the first half of P while the softmax finishes the second
+                    if (!mbar_wait(&phalf[t], j & 1, abort_flag)) { ok = false; break; }
+                    tc_fence_after();
+                    issue_pv(t, j, 0);
                     if (!mbar_wait(&pready[t], j & 1, abort_flag)) { ok = false; break; }
                     tc_fence_after();
-                    issue_pv(t, j);
-                    if (j + 1 == nt[t]) mma_commit(&ofinal[t]);
-                    if (j + 1 < nt[t]) {
+                    issue_pv(t, j, 1);
+                    if (j + 1 == ntt) mma_commit(&ofinal[t]);
+                    if (j + 1 < ntt) {
                         if (!have_next_k) {
                             if (!mbar_wait(&kfull[(j + 1) & 1], ((j + 1) >> 1) & 1, abort_flag)) {
                                 ok = false;
@@ -244,14 +279,16 @@ fmha_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
         const int t = warp >> 2;
         const int quarter = warp & 3;
         const int r = quarter * 32 + lane;
-        const int qrow = q0[t] + r;
+        const int tq0 = t ? q01 : q00;        // first query row of this tile
+        const int tnt = t ? nt1 : nt0;        // key tiles this tile needs
+        const int qrow = tq0 + r;
         const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
         const uint32_t s_addr = tmem_base + lane_off + (t ? C::S_COL1 : C::S_COL0);
         const uint32_t o_addr = tmem_base + lane_off + (t ? C::O_COL1 : C::O_COL0);
         const float c = p.scale_log2;
         float m_used = -INFINITY, l = 0.f;
         bool alive = true;
-        for (int j = 0; j < nt[t]; j++) {
+        for (int j = 0; j < tnt; j++) {
             if (!mbar_wait(&sfull[t], j & 1, abort_flag)) { alive = false; break; }
             tc_fence_after();
             float s[BKEY];
@@ -260,16 +297,21 @@ fmha_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
                 tmem_ld32(s_addr + c0, *reinterpret_cast<uint32_t(*)[32]>(&s[c0]));
             tmem_wait_ld();
             const int key0 = j * BKEY;
-            const bool edge = (key0 + BKEY > p.sk) || (p.causal && key0 + BKEY - 1 > q0[t] + p.diag);
+            const bool edge = (key0 + BKEY > p.sk) || (p.causal && key0 + BKEY - 1 > tq0 + p.diag);
             if (edge) {
                 const int lim = p.causal ? min(p.sk - 1, qrow + p.diag) : p.sk - 1;
 #pragma unroll
                 for (int i = 0; i < BKEY; i++)
                     if (key0 + i > lim) s[i] = -INFINITY;
             }
-            float mx = s[0];
+            // row max over 8 independent partial maxima (short dependency chains)
+            float mx8[8];
 #pragma unroll
-            for (int i = 1; i < BKEY; i++) mx = fmaxf(mx, s[i]);
+            for (int i = 0; i < 8; i++) mx8[i] = s[i];
+#pragma unroll
+            for (int i = 8; i < BKEY; i++) mx8[i & 7] = fmaxf(mx8[i & 7], s[i]);
+            const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                                   fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
             const float m_new = fmaxf(m_used, mx);
             if (j == 0) {
                 m_used = m_new;
@@ -295,26 +337,42 @@ fmha_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
                 }
             }
             const float mc = m_used == -INFINITY ? 0.f : m_used * c;
-            float sum = 0.f;
+            // exponentials: one column pair in POLY on the FMA pipe
+            // (ex2_poly), the rest on MUFU; row sum over 8 partial sums
+            float sum8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
             uint32_t pk[BKEY / 2];
+            // two halves of the keys: P of keys 0-63 is stored and announced
+            // (phalf) before the exponentials of keys 64-127, so P.V starts
+            // while this warp is still working
 #pragma unroll
-            for (int i = 0; i < BKEY / 2; i++) {
-                const float p0 = ex2(fmaf(s[2 * i], c, -mc));
-                const float p1 = ex2(fmaf(s[2 * i + 1], c, -mc));
-                sum += p0 + p1;
-                pk[i] = pack2<BF16>(p0, p1);
+            for (int half = 0; half < 2; half++) {
+#pragma unroll
+                for (int i = half * (BKEY / 4); i < (half + 1) * (BKEY / 4); i++) {
+                    const float x0 = fmaf(s[2 * i], c, -mc), x1 = fmaf(s[2 * i + 1], c, -mc);
+                    float p0, p1;
+                    if (POLY > 0 && i % (POLY > 0 ? POLY : 1) == (POLY > 0 ? POLY : 1) - 1) {
+                        p0 = ex2_poly(x0);
+                        p1 = ex2_poly(x1);
+                    } else {
+                        p0 = ex2(x0);
+                        p1 = ex2(x1);
+                    }
+                    sum8[i & 7] += p0 + p1;
+                    pk[i] = pack2<BF16>(p0, p1);
+                }
+#pragma unroll
+                for (int c0 = half * (BKEY / 4); c0 < (half + 1) * (BKEY / 4); c0 += 16)
+                    tmem_st16(s_addr + c0, *reinterpret_cast<uint32_t(*)[16]>(&pk[c0]));
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(half ? &pready[t] : &phalf[t]);
             }
-            l += sum;
-#pragma unroll
-            for (int c0 = 0; c0 < BKEY / 2; c0 += 16)
-                tmem_st16(s_addr + c0, *reinterpret_cast<uint32_t(*)[16]>(&pk[c0]));
-            tmem_wait_st();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&pready[t]);
+            l += ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) +
+                 ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
         }
         // ---- epilogue: O / l -> 16-bit, LSE ----
-        bool have_o = nt[t] > 0 && alive;
+        bool have_o = tnt > 0 && alive;
         if (have_o) {
             if (!mbar_wait(&ofinal[t], 0, abort_flag)) have_o = false;
             else tc_fence_after();
@@ -396,11 +454,11 @@ bool attn_tmap(CUtensorMap* tm, int elem, const void* base, int d, int seq, int 
     return r == CUDA_SUCCESS;
 }
 
-template <int D, bool BF16>
-int launch(const AttnDesc& d, const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v,
+template <int D, bool BF16, int POLY>
+int launch_poly(const AttnDesc& d, const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v,
            const FParams& p, long long grid, cudaStream_t s) {
     using C = FCfg<D>;
-    auto kern = fmha_fwd_kernel<D, BF16>;
+    auto kern = fmha_fwd_kernel<D, BF16, POLY>;
     static std::atomic<unsigned long long> attr_set{0};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -414,6 +472,28 @@ int launch(const AttnDesc& d, const CUtensorMap& q, const CUtensorMap& k, const 
     cudaError_t e = cudaGetLastError();
     if (e == cudaSuccess) note_launch();
     return e == cudaSuccess ? 0 : (int)e;
+}
+
+// Share of the exponentials computed by polynomial: ZBLAS_FMHA_POLY = 0 (all
+// on MUFU), 4 or 8 (one column pair in 4 or 8); default 0.
+int poly_share() {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("ZBLAS_FMHA_POLY");
+        const int x = e ? atoi(e) : 0;
+        v = (x == 4 || x == 8) ? x : 0;
+    }
+    return v;
+}
+
+template <int D, bool BF16>
+int launch(const AttnDesc& d, const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v,
+           const FParams& p, long long grid, cudaStream_t s) {
+    switch (poly_share()) {
+    case 4: return launch_poly<D, BF16, 4>(d, q, k, v, p, grid, s);
+    case 8: return launch_poly<D, BF16, 8>(d, q, k, v, p, grid, s);
+    default: return launch_poly<D, BF16, 0>(d, q, k, v, p, grid, s);
+    }
 }
 
 bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
