@@ -30,6 +30,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <mutex>
+#include <string>
 
 namespace zl {
 
@@ -113,6 +114,7 @@ __device__ __forceinline__ void decode_tile(int t, int tiles_m, int tiles_n,
 template <bool MN, int ROWS, int BK, int BOX>
 __device__ __forceinline__ void load_operand(uint8_t* dst, const CUtensorMap* tm,
                                              uint64_t* bar, int mn0, int k0, int b) {
+    static_assert(!MN || ROWS % BOX == 0, "an MN-major tile is made of whole swizzle rows");
     if constexpr (!MN) {
         tma_load_3d(dst, tm, bar, k0, mn0, b);
     } else {
@@ -127,6 +129,7 @@ __device__ __forceinline__ void load_operand(uint8_t* dst, const CUtensorMap* tm
 template <bool MN, int ROWS, int BK, int BOX>
 __device__ __forceinline__ void load_operand_pair(uint8_t* dst, const CUtensorMap* tm,
                                                   uint32_t bar0, int mn0, int k0, int b) {
+    static_assert(!MN || ROWS % BOX == 0, "an MN-major tile is made of whole swizzle rows");
     if constexpr (!MN) {
         tma_load_3d_pair(dst, tm, bar0, k0, mn0, b);
     } else {
@@ -614,9 +617,11 @@ struct Maps {
 };
 
 // Kinds and widths the CTA-pair kernel is built for.
+// (each CTA holds BN/2 columns of B; an MN-major int8 swizzle row is 128
+// columns wide, so int8 pairs need BN = 256)
 constexpr bool pair_ok(int kind, int bn) {
-    return bn == 256 && (kind == (int)Kind::F16 || kind == (int)Kind::BF16 ||
-                         kind == (int)Kind::I8);
+    return (bn == 256 && kind == (int)Kind::I8) ||
+           ((bn == 256 || bn == 128) && (kind == (int)Kind::F16 || kind == (int)Kind::BF16));
 }
 
 template <int KIND, int BN, bool A_MN, bool B_MN, int OUT, bool EPI_TMA, bool PAIR>
@@ -755,26 +760,51 @@ int gemm_tc(const GemmDesc& d, cudaStream_t s) {
     const bool b_mn = d.transb != 0;     // op(B)(l,j) = B[j + l*ldb]: N contiguous
     const int bk = 128 / es, box = 128 / es;
 
-    // tile width: 256 columns when that still fills the GPU
+    // Tile configuration.  fp16/bf16/int8: the candidate with the least
+    // estimated time, waves * tile area / (SMs per tile * per-SM speed); the
+    // speeds are B200 measurements of each configuration at 8192^3 (pair of
+    // 256x256 tiles 1.00, single 128x256 0.90, single 128x128 0.69).  Pairs
+    // need K >= 2048 bytes (short K: the pair's extra synchronisation
+    // outweighs the halved B loads).  fp32 forms: 128 (or 64) wide tiles.
     const int sms = num_sms();
-    const long long tiles256 = (long long)((d.m + BM - 1) / BM) * ((d.n + 255) / 256) * d.batch;
-    int BN = 256;
-    if (d.kind == Kind::TF32X3) BN = 128;
-    else if (tiles256 < sms && d.n > 128) BN = 128;
-    else if (d.n <= 128) BN = 128;
-    if (d.kind == Kind::TF32X3) {
-        const long long tiles128 = (long long)((d.m + BM - 1) / BM) * ((d.n + 127) / 128) * d.batch;
-        if (tiles128 < sms) BN = 64;
-    }
-
     Maps maps;
-    // CTA pairs (256-row tiles, B split between the two SMs) when there are
-    // enough pair tiles to occupy the GPU
-    const long long pair_tiles =
-        (long long)((d.m + 2 * BM - 1) / (2 * BM)) * ((d.n + BN - 1) / BN) * d.batch;
-    // (short K: the pair's extra synchronisation outweighs the halved B loads)
-    maps.pair = pair_ok((int)d.kind, BN) && !getenv("ZBLAS_NO_PAIR") && pair_tiles >= sms / 2 &&
-                (long long)d.k * es >= 2048;
+    maps.pair = false;
+    int BN = 128;
+    if (d.kind == Kind::TF32X3 || d.kind == Kind::TF32) {
+        const long long tiles256 = (long long)((d.m + BM - 1) / BM) * ((d.n + 255) / 256) * d.batch;
+        BN = (d.kind == Kind::TF32 && tiles256 >= sms && d.n > 128) ? 256 : 128;
+        if (d.kind == Kind::TF32X3) {
+            const long long tiles128 = (long long)((d.m + BM - 1) / BM) * ((d.n + 127) / 128) * d.batch;
+            if (tiles128 < sms) BN = 64;
+        }
+    } else {
+        struct Cand { int bn; bool pair; double speed; };
+        const Cand cands[3] = {{256, true, 1.00}, {256, false, 0.90}, {128, false, 0.69}};
+        double best = 0.0;
+        for (const Cand& c : cands) {
+            if (c.pair && (getenv("ZBLAS_NO_PAIR") || (long long)d.k * es < 2048)) continue;
+            const int rows = c.pair ? 2 * BM : BM;
+            const long long tiles =
+                (long long)((d.m + rows - 1) / rows) * ((d.n + c.bn - 1) / c.bn) * d.batch;
+            const long long slots = c.pair ? sms / 2 : sms;
+            const long long waves = (tiles + slots - 1) / slots;
+            const double cost = (double)waves * rows * c.bn / ((c.pair ? 2.0 : 1.0) * c.speed);
+            if (best == 0.0 || cost < best) {
+                best = cost;
+                BN = c.bn;
+                maps.pair = c.pair;
+            }
+        }
+    }
+    if (const char* f = getenv("ZBLAS_GEMM_CFG")) {      // forced tile configuration
+        if (pair_ok((int)d.kind, 256)) {
+            const std::string cfg(f);
+            if (cfg == "s128") { BN = 128; maps.pair = false; }
+            if (cfg == "s256") { BN = 256; maps.pair = false; }
+            if (cfg == "p128" && pair_ok((int)d.kind, 128)) { BN = 128; maps.pair = true; }
+            if (cfg == "p256") { BN = 256; maps.pair = true; }
+        }
+    }
     const int b_rows = maps.pair ? BN / 2 : BN;
     CUtensorMap &ta = maps.a, &tb = maps.b, &ta2 = maps.a2, &tb2 = maps.b2;
     auto mk = [&](CUtensorMap* tm, const void* base, bool mn, long long mn_ext, long long ld,
