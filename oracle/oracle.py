@@ -65,6 +65,8 @@ def oracle() -> ctypes.CDLL:
         lib.zo_gemm_entries.restype = None
         lib.zo_gemm_entries.argtypes = [_int, _int, _int, _d, _vp, _int, _int, _vp, _int,
                                         _int, _d, _vp, _int, _int, _vp, _vp, _ll, _vp]
+        lib.zo_lt_epilogue.restype = None
+        lib.zo_lt_epilogue.argtypes = [_vp, _int, _int, _int, _int, _ll, _int, _vp, _int]
         lib.zo_attention.restype = _int
         lib.zo_attention.argtypes = [ctypes.POINTER(AttnDesc)]
         lib.zo_attention_rows.restype = _int
@@ -125,6 +127,12 @@ def gemm_strided_batched_ex(transa, transb, m, n, k, alpha, A, Atype, lda, sA, B
     return oracle().zo_gemm_strided_batched_ex(transa, transb, m, n, k, _p(al), _p(A), Atype,
                                                lda, sA, _p(B), Btype, ldb, sB, _p(be), _p(C),
                                                Ctype, ldc, sC, batch, compute)
+
+
+def lt_epilogue(D, Dtype, m, n, ldd, strideD, batch, bias, flags) -> None:
+    """The reference's cublasLtMatmul epilogue on host D (in place)."""
+    oracle().zo_lt_epilogue(_p(D), Dtype, m, n, ldd, strideD, batch,
+                            _p(bias) if bias is not None else None, flags)
 
 
 def gemm_entries(transa, transb, k, alpha, A, Atype, lda, B, Btype, ldb, beta, C0, Ctype, ldc,

@@ -24,6 +24,8 @@
  *       arithmetic with two's-complement wrap for alpha/beta scaling.
  *   zo_gemm_strided_batched_ex            zblas/zblas.c:491-511 (host loop
  *       over the batch; strides in elements, elem_size :488-490).
+ *   zo_lt_epilogue                        cublasLtMatmul's bias / ReLU /
+ *       GELU pass, zblas/zblas.c:692-710 with gelu_tanh :638-642.
  *   zo_attention / zo_attention_rows      the fp32 math of fmha_f32
  *       (zblas/zblas_gpu.cpp:793-844) with the masking and rounding points
  *       of fmha_run (zblas/zblas_gpu.cpp:892-1039): causal mask
@@ -281,6 +283,37 @@ void zo_gemm_entries(int transa, int transb, int k, double alpha,
         double c = alpha * acc;
         if (beta != 0.0 && C0) c += beta * load_elem(C0, Ctype, i + j * (int64_t)ldc);
         out[t] = c;
+    }
+}
+
+/* cublasLtMatmul's epilogue as the reference applies it after the GEMM
+ * (zblas/zblas.c:692-710): D (already narrowed) is widened, bias[row] added
+ * (bias in D's 16-bit type, fp32 otherwise), ReLU or tanh-form GELU applied
+ * (zblas.c:638-642), and narrowed again.  flags: 1 bias, 2 relu, 4 gelu. */
+static float zo_gelu_tanh(float x) {
+    const float c = 0.7978845608028654f;
+    float inner = c * (x + 0.044715f * x * x * x);
+    return 0.5f * x * (1.0f + tanhf(inner));
+}
+
+void zo_lt_epilogue(void *D, int Dtype, int m, int n, int ldd, long long strideD, int batch,
+                    const void *bias, int flags) {
+    for (int b = 0; b < batch; b++) {
+        for (int j = 0; j < n; j++) {
+            for (int i = 0; i < m; i++) {
+                int64_t at = (int64_t)b * strideD + i + (int64_t)j * ldd;
+                float v = (float)load_elem(D, Dtype, at);
+                if ((flags & 1) && bias) {
+                    int bt = (Dtype == ZO_R_16F || Dtype == ZO_R_16BF) ? Dtype : ZO_R_32F;
+                    v += (float)load_elem(bias, bt, i);
+                }
+                if ((flags & 2) && v < 0.0f) v = 0.0f;
+                if (flags & 4) v = zo_gelu_tanh(v);
+                if (Dtype == ZO_R_16F) ((uint16_t *)D)[at] = zo_float_to_half(v);
+                else if (Dtype == ZO_R_16BF) ((uint16_t *)D)[at] = zo_float_to_bf16(v);
+                else ((float *)D)[at] = v;
+            }
+        }
     }
 }
 

@@ -14,7 +14,7 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 def _declared():
     names = set()
-    for h in ("zlift_cublas.h", "zlift_attention.h", "zlift_partition.h"):
+    for h in ("zlift_cublas.h", "zlift_cublaslt.h", "zlift_attention.h", "zlift_partition.h"):
         lines = open(os.path.join(ROOT, "include", h)).read().splitlines()
         src = "\n".join(l for l in lines if not l.lstrip().startswith("#"))
         for m in re.finditer(r"ZLIFT_API\s+[^;(]*?\b(\w+)\s*\(", src):

@@ -8,6 +8,7 @@
 #include "gemm.h"
 
 #include "../../include/zlift_cublas.h"
+#include "../../include/zlift_cublaslt.h"
 
 #include <cuda_fp16.h>
 
@@ -101,8 +102,7 @@ static cublasStatus_t map_launch(int rc) {
 
 // Runs one validated GEMM description: tensor cores first, CUDA cores when
 // the layout is outside what TMA can describe.
-static cublasStatus_t run_gemm(Handle* h, GemmDesc& d) {
-    cudaStream_t s = h->stream;
+static cublasStatus_t run_gemm(Handle* h, GemmDesc& d, cudaStream_t s) {
     if (d.m == 0 || d.n == 0 || d.batch == 0) return CUBLAS_STATUS_SUCCESS;
     if (d.k == 0) return map_launch(gemm_simt(d, s));   // C = beta*C
     if (d.kind == Kind::TF32X3 || d.kind == Kind::TF32) {
@@ -162,13 +162,13 @@ static cublasStatus_t check_dims(int transa, int transb, int m, int n, int k,
 }
 
 // Reads the scalars according to the pointer mode.  32F: float; 32I: int32.
-static cublasStatus_t set_scalars(Handle* h, GemmDesc& d, const void* alpha,
+static cublasStatus_t set_scalars(int pointer_mode, GemmDesc& d, const void* alpha,
                                   const void* beta, bool integer) {
     if (!alpha || !beta) return CUBLAS_STATUS_INVALID_VALUE;
     d.alpha_dev = d.beta_dev = nullptr;
     d.alpha = d.beta = 0.f;
     d.ialpha = d.ibeta = 0;
-    if (h->pointer_mode == CUBLAS_POINTER_MODE_DEVICE) {
+    if (pointer_mode == CUBLAS_POINTER_MODE_DEVICE) {
         d.alpha_dev = alpha;
         d.beta_dev = beta;
     } else if (integer) {
@@ -181,13 +181,24 @@ static cublasStatus_t set_scalars(Handle* h, GemmDesc& d, const void* alpha,
     return CUBLAS_STATUS_SUCCESS;
 }
 
+// What cublasLtMatmul adds to a GEMM call: a fused epilogue, its own
+// stream and its own pointer mode.
+struct LtExtra {
+    int epi;
+    const void* bias;
+    int bias_type;
+    cudaStream_t stream;
+    int pointer_mode;
+};
+
 // Type/compute dispatch of cublasGemmEx (zblas/zblas.c:357-391) for one
 // (possibly batched) call.
 static cublasStatus_t gemm_ex(Handle* h, int transa, int transb, int m, int n, int k,
                               const void* alpha, const void* A, int Atype, int lda,
                               long long sA, const void* B, int Btype, int ldb,
                               long long sB, const void* beta, void* C, int Ctype,
-                              int ldc, long long sC, int batch, int computeType) {
+                              int ldc, long long sC, int batch, int computeType,
+                              const LtExtra* lt = nullptr) {
     cublasStatus_t st = check_dims(transa, transb, m, n, k, lda, ldb, ldc);
     if (st) return st;
     if (batch < 0) return CUBLAS_STATUS_INVALID_VALUE;
@@ -216,13 +227,19 @@ static cublasStatus_t gemm_ex(Handle* h, int transa, int transb, int m, int n, i
             return CUBLAS_STATUS_NOT_SUPPORTED;
         }
     }
+    if (lt && lt->epi && integer) return CUBLAS_STATUS_NOT_SUPPORTED;
     if (m == 0 || n == 0 || batch == 0) return CUBLAS_STATUS_SUCCESS;
     if (!C || (k > 0 && (!A || !B))) return CUBLAS_STATUS_INVALID_VALUE;
-    st = set_scalars(h, d, alpha, beta, integer);
+    st = set_scalars(lt ? lt->pointer_mode : h->pointer_mode, d, alpha, beta, integer);
     if (st) return st;
-    trace("gemm kind=%d %dx%dx%d batch=%d ta=%d tb=%d lda=%d ldb=%d ldc=%d", (int)d.kind, m, n,
-          k, batch, transa, transb, lda, ldb, ldc);
-    return run_gemm(h, d);
+    if (lt) {
+        d.epi = lt->epi;
+        d.bias = lt->bias;
+        d.bias_type = lt->bias_type;
+    }
+    trace("gemm kind=%d %dx%dx%d batch=%d ta=%d tb=%d lda=%d ldb=%d ldc=%d epi=%d", (int)d.kind,
+          m, n, k, batch, transa, transb, lda, ldb, ldc, d.epi);
+    return run_gemm(h, d, lt ? lt->stream : h->stream);
 }
 
 }  // namespace zl
@@ -426,6 +443,254 @@ cublasStatus_t cublasHgemm(cublasHandle_t handle, int transa, int transb, int m,
     return gemm_ex(h, transa, transb, m, n, k, &fa, A, kR16F, lda, 0, B, kR16F, ldb, 0, &fb, C,
                    kR16F, ldc, 0, 1, CUBLAS_COMPUTE_32F);
 }
+
+// ---- cuBLASLt subset (zblas/zblas.c:512-711) ---------------------------
+
+}  // extern "C"
+
+namespace {
+
+struct LtDesc {
+    unsigned magic = 0x4c746465;    // "Ltde"
+    int compute_type = 0, scale_type = 0, pointer_mode = 0;
+    int transa = 0, transb = 0, epilogue = CUBLASLT_EPILOGUE_DEFAULT;
+    const void* bias = nullptr;
+};
+
+struct LtLayout {
+    unsigned magic = 0x4c746c61;    // "Ltla"
+    int type = 0, order = CUBLASLT_ORDER_COL;
+    long long rows = 0, cols = 0, ld = 0;
+    int batch = 1;
+    long long batch_stride = 0;
+};
+
+LtDesc* as_desc(void* p) {
+    LtDesc* d = static_cast<LtDesc*>(p);
+    return d && d->magic == 0x4c746465 ? d : nullptr;
+}
+LtLayout* as_layout(void* p) {
+    LtLayout* l = static_cast<LtLayout*>(p);
+    return l && l->magic == 0x4c746c61 ? l : nullptr;
+}
+
+template <typename T>
+cublasStatus_t put(T& field, const void* buf, size_t bytes) {
+    if (bytes < sizeof(T)) return CUBLAS_STATUS_INVALID_VALUE;
+    std::memcpy(&field, buf, sizeof(T));
+    return CUBLAS_STATUS_SUCCESS;
+}
+
+}  // namespace
+
+extern "C" {
+
+cublasStatus_t cublasLtCreate(cublasLtHandle_t* handle) { return cublasCreate_v2(handle); }
+cublasStatus_t cublasLtDestroy(cublasLtHandle_t handle) { return cublasDestroy_v2(handle); }
+cublasStatus_t cublasLtGetVersion(void) { return 130100; }
+
+cublasStatus_t cublasLtMatmulDescCreate(void** desc, int computeType, int scaleType) {
+    if (!desc) return CUBLAS_STATUS_INVALID_VALUE;
+    LtDesc* d = new (std::nothrow) LtDesc();
+    if (!d) return CUBLAS_STATUS_NOT_INITIALIZED;
+    d->compute_type = computeType;
+    d->scale_type = scaleType;
+    *desc = d;
+    return CUBLAS_STATUS_SUCCESS;
+}
+
+cublasStatus_t cublasLtMatmulDescDestroy(void* desc) {
+    LtDesc* d = as_desc(desc);
+    if (d) {
+        d->magic = 0;
+        delete d;
+    }
+    return CUBLAS_STATUS_SUCCESS;
+}
+
+cublasStatus_t cublasLtMatmulDescSetAttribute(void* desc, int attr, const void* buf,
+                                              size_t bytes) {
+    LtDesc* d = as_desc(desc);
+    if (!d || !buf) return CUBLAS_STATUS_INVALID_VALUE;
+    switch (attr) {
+    case CUBLASLT_MATMUL_DESC_COMPUTE_TYPE: return put(d->compute_type, buf, bytes);
+    case CUBLASLT_MATMUL_DESC_SCALE_TYPE: return put(d->scale_type, buf, bytes);
+    case CUBLASLT_MATMUL_DESC_POINTER_MODE: return put(d->pointer_mode, buf, bytes);
+    case CUBLASLT_MATMUL_DESC_TRANSA: return put(d->transa, buf, bytes);
+    case CUBLASLT_MATMUL_DESC_TRANSB: return put(d->transb, buf, bytes);
+    case CUBLASLT_MATMUL_DESC_EPILOGUE: return put(d->epilogue, buf, bytes);
+    case CUBLASLT_MATMUL_DESC_BIAS_POINTER: return put(d->bias, buf, bytes);
+    default: return CUBLAS_STATUS_SUCCESS;   // accepted and ignored, as in zblas.c:563
+    }
+}
+
+cublasStatus_t cublasLtMatmulDescGetAttribute(void* desc, int attr, void* buf, size_t bytes,
+                                              size_t* written) {
+    LtDesc* d = as_desc(desc);
+    if (!d || !buf) return CUBLAS_STATUS_INVALID_VALUE;
+    if (attr == CUBLASLT_MATMUL_DESC_BIAS_POINTER) {
+        if (bytes < sizeof(void*)) return CUBLAS_STATUS_INVALID_VALUE;
+        std::memcpy(buf, &d->bias, sizeof(void*));
+        if (written) *written = sizeof(void*);
+        return CUBLAS_STATUS_SUCCESS;
+    }
+    int v = attr == CUBLASLT_MATMUL_DESC_TRANSA ? d->transa
+          : attr == CUBLASLT_MATMUL_DESC_TRANSB ? d->transb
+          : attr == CUBLASLT_MATMUL_DESC_EPILOGUE ? d->epilogue
+          : attr == CUBLASLT_MATMUL_DESC_COMPUTE_TYPE ? d->compute_type
+          : attr == CUBLASLT_MATMUL_DESC_SCALE_TYPE ? d->scale_type
+          : attr == CUBLASLT_MATMUL_DESC_POINTER_MODE ? d->pointer_mode : 0;
+    if (bytes < sizeof v) return CUBLAS_STATUS_INVALID_VALUE;
+    std::memcpy(buf, &v, sizeof v);
+    if (written) *written = sizeof v;
+    return CUBLAS_STATUS_SUCCESS;
+}
+
+cublasStatus_t cublasLtMatrixLayoutCreate(void** layout, int type, unsigned long long rows,
+                                          unsigned long long cols, long long ld) {
+    if (!layout) return CUBLAS_STATUS_INVALID_VALUE;
+    LtLayout* l = new (std::nothrow) LtLayout();
+    if (!l) return CUBLAS_STATUS_NOT_INITIALIZED;
+    l->type = type;
+    l->rows = (long long)rows;
+    l->cols = (long long)cols;
+    l->ld = ld;
+    *layout = l;
+    return CUBLAS_STATUS_SUCCESS;
+}
+
+cublasStatus_t cublasLtMatrixLayoutDestroy(void* layout) {
+    LtLayout* l = as_layout(layout);
+    if (l) {
+        l->magic = 0;
+        delete l;
+    }
+    return CUBLAS_STATUS_SUCCESS;
+}
+
+cublasStatus_t cublasLtMatrixLayoutSetAttribute(void* layout, int attr, const void* buf,
+                                                size_t bytes) {
+    LtLayout* l = as_layout(layout);
+    if (!l || !buf) return CUBLAS_STATUS_INVALID_VALUE;
+    switch (attr) {
+    case CUBLASLT_MATRIX_LAYOUT_TYPE: return put(l->type, buf, bytes);
+    case CUBLASLT_MATRIX_LAYOUT_ORDER: return put(l->order, buf, bytes);
+    case CUBLASLT_MATRIX_LAYOUT_ROWS: {
+        unsigned long long v;
+        cublasStatus_t st = put(v, buf, bytes);
+        if (!st) l->rows = (long long)v;
+        return st;
+    }
+    case CUBLASLT_MATRIX_LAYOUT_COLS: {
+        unsigned long long v;
+        cublasStatus_t st = put(v, buf, bytes);
+        if (!st) l->cols = (long long)v;
+        return st;
+    }
+    case CUBLASLT_MATRIX_LAYOUT_LD: return put(l->ld, buf, bytes);
+    case CUBLASLT_MATRIX_LAYOUT_BATCH_COUNT: return put(l->batch, buf, bytes);
+    case CUBLASLT_MATRIX_LAYOUT_STRIDED_BATCH_OFFSET: return put(l->batch_stride, buf, bytes);
+    default: return CUBLAS_STATUS_SUCCESS;
+    }
+}
+
+cublasStatus_t cublasLtMatmulPreferenceCreate(void** pref) {
+    if (!pref) return CUBLAS_STATUS_INVALID_VALUE;
+    void* p = calloc(1, 8);
+    if (!p) return CUBLAS_STATUS_NOT_INITIALIZED;
+    *pref = p;
+    return CUBLAS_STATUS_SUCCESS;
+}
+
+cublasStatus_t cublasLtMatmulPreferenceDestroy(void* pref) {
+    free(pref);
+    return CUBLAS_STATUS_SUCCESS;
+}
+
+cublasStatus_t cublasLtMatmulPreferenceSetAttribute(void* pref, int, const void*, size_t) {
+    return pref ? CUBLAS_STATUS_SUCCESS : CUBLAS_STATUS_INVALID_VALUE;
+}
+
+// One "algorithm": the library picks its tile configuration per call.
+cublasStatus_t cublasLtMatmulAlgoGetHeuristic(void*, void*, void*, void*, void*, void*, void*,
+                                              int requested, void* results, int* returned) {
+    if (!results || !returned || requested < 1) return CUBLAS_STATUS_INVALID_VALUE;
+    zlift_lt_heuristic_result* r = static_cast<zlift_lt_heuristic_result*>(results);
+    std::memset(r, 0, sizeof *r);
+    r->state = CUBLAS_STATUS_SUCCESS;
+    r->wavesCount = 1.0f;
+    *returned = 1;
+    return CUBLAS_STATUS_SUCCESS;
+}
+
+cublasStatus_t cublasLtMatmul(void* lt, void* desc, const void* alpha, const void* A,
+                              void* Adesc, const void* B, void* Bdesc, const void* beta,
+                              const void* C, void* Cdesc, void* D, void* Ddesc, const void* algo,
+                              void* workspace, size_t workspaceBytes, void* stream) {
+    (void)algo; (void)workspace; (void)workspaceBytes;
+    Handle* h = as_handle(lt);
+    if (!h) return CUBLAS_STATUS_NOT_INITIALIZED;
+    LtDesc* d = as_desc(desc);
+    LtLayout *la = as_layout(Adesc), *lb = as_layout(Bdesc), *ld_ = as_layout(Ddesc);
+    LtLayout* lc = Cdesc ? as_layout(Cdesc) : ld_;
+    if (!d || !la || !lb || !ld_ || !lc) return CUBLAS_STATUS_INVALID_VALUE;
+    if (la->order != CUBLASLT_ORDER_COL || lb->order != CUBLASLT_ORDER_COL ||
+        lc->order != CUBLASLT_ORDER_COL || ld_->order != CUBLASLT_ORDER_COL)
+        return CUBLAS_STATUS_NOT_SUPPORTED;
+    const long long m = ld_->rows, n = ld_->cols;
+    const long long k = d->transa == CUBLAS_OP_N ? la->cols : la->rows;
+    const bool a_ok = d->transa == CUBLAS_OP_N ? la->rows == m : la->cols == m;
+    const bool b_ok = d->transb == CUBLAS_OP_N ? (lb->rows == k && lb->cols == n)
+                                               : (lb->rows == n && lb->cols == k);
+    if (!a_ok || !b_ok || lc->rows != m || lc->cols != n) return CUBLAS_STATUS_INVALID_VALUE;
+    if (m > 0x7fffffffLL || n > 0x7fffffffLL || k > 0x7fffffffLL)
+        return CUBLAS_STATUS_NOT_SUPPORTED;
+    const int batch = ld_->batch;
+    if (la->batch != batch || lb->batch != batch || lc->batch != batch)
+        return CUBLAS_STATUS_NOT_SUPPORTED;
+    if (lc->type != ld_->type) return CUBLAS_STATUS_NOT_SUPPORTED;
+    LtExtra x{};
+    switch (d->epilogue) {
+    case CUBLASLT_EPILOGUE_DEFAULT: x.epi = 0; break;
+    case CUBLASLT_EPILOGUE_RELU: x.epi = kEpiRelu; break;
+    case CUBLASLT_EPILOGUE_BIAS: x.epi = kEpiBias; break;
+    case CUBLASLT_EPILOGUE_RELU_BIAS: x.epi = kEpiBias | kEpiRelu; break;
+    case CUBLASLT_EPILOGUE_GELU: x.epi = kEpiGelu; break;
+    case CUBLASLT_EPILOGUE_GELU_BIAS: x.epi = kEpiBias | kEpiGelu; break;
+    default: return CUBLAS_STATUS_NOT_SUPPORTED;
+    }
+    if ((x.epi & kEpiBias) && !d->bias) return CUBLAS_STATUS_INVALID_VALUE;
+    x.bias = d->bias;
+    // bias in the output's 16-bit type, fp32 otherwise (zblas.c:696-704)
+    x.bias_type = (ld_->type == kR16F || ld_->type == kR16BF) ? ld_->type : kR32F;
+    x.stream = static_cast<cudaStream_t>(stream);
+    x.pointer_mode = d->pointer_mode;
+    // C != D: D starts as a copy of C (zblas.c:681-686), on the call's stream
+    if (C && C != D && m > 0 && n > 0) {
+        const size_t es = elem_size(ld_->type);
+        for (int b = 0; b < batch; b++) {
+            const char* src = static_cast<const char*>(C) + (size_t)b * lc->batch_stride * es;
+            char* dst = static_cast<char*>(D) + (size_t)b * ld_->batch_stride * es;
+            if (cudaMemcpy2DAsync(dst, ld_->ld * es, src, lc->ld * es, m * es, n,
+                                  cudaMemcpyDeviceToDevice, x.stream) != cudaSuccess) {
+                cudaGetLastError();
+                return CUBLAS_STATUS_EXECUTION_FAILED;
+            }
+        }
+    }
+    const int compute = d->compute_type ? d->compute_type : kR32F;
+    return gemm_ex(h, d->transa, d->transb, (int)m, (int)n, (int)k, alpha, A, la->type,
+                   (int)la->ld, la->batch_stride, B, lb->type, (int)lb->ld, lb->batch_stride,
+                   beta, D, ld_->type, (int)ld_->ld, ld_->batch_stride, batch, compute, &x);
+}
+
+#define ZLIFT_DEFINE_UNSUPPORTED(name)                       \
+    cublasStatus_t name(void) {                              \
+        trace("unsupported: %s", #name);                     \
+        return CUBLAS_STATUS_NOT_SUPPORTED;                  \
+    }
+ZLIFT_UNSUPPORTED_LIST(ZLIFT_DEFINE_UNSUPPORTED)
+#undef ZLIFT_DEFINE_UNSUPPORTED
 
 int zlift_device_error(void) {
     cudaDeviceSynchronize();

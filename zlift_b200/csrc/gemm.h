@@ -1,6 +1,7 @@
 // gemm.h -- internal interface between the cuBLAS-style C ABI
 // (cublas_api.cpp) and the GEMM kernels (gemm_tc.cu, gemm_simt.cu).
 #pragma once
+#include <cmath>
 #include <cstdint>
 #include <cuda_runtime.h>
 
@@ -44,7 +45,25 @@ struct GemmDesc {
     // the same layout as A and B.  Filled by the caller through split_tf32.
     const float* A_lo; const float* B_lo;
     const float* A_hi; const float* B_hi;
+    // Fused epilogue after alpha*acc + beta*C (floating-point outputs only):
+    // kEpiBias adds bias[row] (a length-m vector of bias_type), then kEpiRelu
+    // or kEpiGelu (tanh form) is applied.
+    int epi;
+    const void* bias;
+    int bias_type;
 };
+
+enum EpiFlags : int { kEpiBias = 1, kEpiRelu = 2, kEpiGelu = 4 };
+
+// x after the fused epilogue (bias already added by the caller if requested)
+__host__ __device__ inline float apply_act(float x, int epi) {
+    if (epi & kEpiRelu) x = x > 0.f ? x : 0.f;
+    if (epi & kEpiGelu) {
+        const float u = 0.7978845608028654f * (x + 0.044715f * x * x * x);
+        x = 0.5f * x * (1.f + tanhf(u));
+    }
+    return x;
+}
 
 // Tensor-core path.  Returns 0 when launched, 1 when this shape/layout is
 // not eligible (the caller then uses the general kernel), or a CUDA error

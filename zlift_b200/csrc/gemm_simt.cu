@@ -31,6 +31,9 @@ struct SimtParams {
     int32_t ia, ib;
     const void* alpha_dev;
     const void* beta_dev;
+    int epi;
+    const void* bias;
+    int bias_type;
 };
 
 __device__ __forceinline__ float ldf(const void* p, int t, long long at) {
@@ -103,6 +106,7 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(const SimtParams p) {
     }
     const long long gi = i0 + tx;
     if (gi >= p.m) return;
+    const float bias_row = (p.epi & kEpiBias) && p.bias ? ldf(p.bias, p.bias_type, gi) : 0.f;
 #pragma unroll
     for (int c = 0; c < 4; c++) {
         const long long gj = j0 + ty + 8 * c;
@@ -118,14 +122,17 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(const SimtParams p) {
             if (p.Ct == kR16F) {
                 __half* cp = static_cast<__half*>(p.C) + at;
                 if (beta != 0.f) v = fmaf(beta, __half2float(*cp), v);
+                if (p.epi) v = apply_act(v + bias_row, p.epi);
                 *cp = __float2half_rn(v);
             } else if (p.Ct == kR16BF) {
                 __nv_bfloat16* cp = static_cast<__nv_bfloat16*>(p.C) + at;
                 if (beta != 0.f) v = fmaf(beta, __bfloat162float(*cp), v);
+                if (p.epi) v = apply_act(v + bias_row, p.epi);
                 *cp = __float2bfloat16_rn(v);
             } else {
                 float* cp = static_cast<float*>(p.C) + at;
                 if (beta != 0.f) v = fmaf(beta, *cp, v);
+                if (p.epi) v = apply_act(v + bias_row, p.epi);
                 *cp = v;
             }
         }
@@ -189,6 +196,9 @@ int gemm_simt(const GemmDesc& d, cudaStream_t s) {
     p.alpha = d.alpha; p.beta = d.beta;
     p.ia = d.ialpha; p.ib = d.ibeta;
     p.alpha_dev = d.alpha_dev; p.beta_dev = d.beta_dev;
+    p.epi = d.kind == Kind::I8 ? 0 : d.epi;
+    p.bias = d.bias;
+    p.bias_type = d.bias_type;
     dim3 grid((d.m + TS - 1) / TS, (d.n + TS - 1) / TS, d.batch);
     if (grid.y > 65535u || grid.z > 65535u) return 1;
     if (d.kind == Kind::I8) gemm_simt_kernel<true><<<grid, 256, 0, s>>>(p);

@@ -58,7 +58,20 @@ struct TcParams {
     int32_t ialpha, ibeta;
     const void* alpha_dev;
     const void* beta_dev;
+    int epi;                 // EpiFlags (floating-point outputs)
+    const void* bias;
+    int bias_type;
 };
+
+// bias[row] as float (0 past the end or without a bias)
+__device__ __forceinline__ float load_bias(const TcParams& p, long long row) {
+    if (!(p.epi & kEpiBias) || !p.bias || row >= p.m) return 0.f;
+    switch (p.bias_type) {
+    case kR16F: return __half2float(static_cast<const __half*>(p.bias)[row]);
+    case kR16BF: return __bfloat162float(static_cast<const __nv_bfloat16*>(p.bias)[row]);
+    default: return static_cast<const float*>(p.bias)[row];
+    }
+}
 
 __host__ __device__ constexpr int out_es(int out) { return (out == kR16F || out == kR16BF) ? 2 : 4; }
 
@@ -173,7 +186,7 @@ __device__ __forceinline__ uint32_t load_c(const void* C, long long at) {
 template <int OUT>
 __device__ __forceinline__ void store_out(void* C, long long at, uint32_t raw, uint32_t old,
                                           bool use_beta, float alpha, float beta,
-                                          int32_t ia, int32_t ib) {
+                                          int32_t ia, int32_t ib, int epi, float bias_row) {
     if constexpr (OUT == kR32I) {
         uint32_t v = (uint32_t)ia * raw;                 // two's-complement wrap
         if (use_beta) v += (uint32_t)ib * old;
@@ -182,13 +195,16 @@ __device__ __forceinline__ void store_out(void* C, long long at, uint32_t raw, u
         float v = alpha * __uint_as_float(raw);
         if constexpr (OUT == kR32F) {
             if (use_beta) v = fmaf(beta, __uint_as_float(old), v);
+            if (epi) v = apply_act(v + bias_row, epi);
             static_cast<float*>(C)[at] = v;
         } else if constexpr (OUT == kR16F) {
             if (use_beta) v = fmaf(beta, __half2float(__ushort_as_half((unsigned short)old)), v);
+            if (epi) v = apply_act(v + bias_row, epi);
             static_cast<__half*>(C)[at] = __float2half_rn(v);
         } else {
             if (use_beta)
                 v = fmaf(beta, __bfloat162float(__ushort_as_bfloat16((unsigned short)old)), v);
+            if (epi) v = apply_act(v + bias_row, epi);
             static_cast<__nv_bfloat16*>(C)[at] = __float2bfloat16_rn(v);
         }
     }
@@ -405,6 +421,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                 const int m0 = tm * TILE_M + (int)rank * BM, n0 = tn * BN;
                 const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
                 const int ncols = min(BN, p.n - n0);
+                const float bias_row = load_bias(p, (long long)m0 + r_in_tile);
 #pragma unroll 1
                 for (int c0 = 0; c0 < ncols; c0 += kEpiCols, chunk++) {
                     const int buf = chunk & 1;
@@ -436,15 +453,18 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                         } else if constexpr (OUT == kR32F) {
                             float x = alpha * __uint_as_float(v[j]);
                             if (use_beta) x = fmaf(beta, *reinterpret_cast<float*>(e), x);
+                            if (p.epi) x = apply_act(x + bias_row, p.epi);
                             *reinterpret_cast<float*>(e) = x;
                         } else if constexpr (OUT == kR16F) {
                             float x = alpha * __uint_as_float(v[j]);
                             if (use_beta) x = fmaf(beta, __half2float(*reinterpret_cast<__half*>(e)), x);
+                            if (p.epi) x = apply_act(x + bias_row, p.epi);
                             *reinterpret_cast<__half*>(e) = __float2half_rn(x);
                         } else {
                             float x = alpha * __uint_as_float(v[j]);
                             if (use_beta)
                                 x = fmaf(beta, __bfloat162float(*reinterpret_cast<__nv_bfloat16*>(e)), x);
+                            if (p.epi) x = apply_act(x + bias_row, p.epi);
                             *reinterpret_cast<__nv_bfloat16*>(e) = __float2bfloat16_rn(x);
                         }
                     }
@@ -473,6 +493,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                 const bool row_ok = row < p.m;
                 const int n0 = tn * BN;
                 const long long base = (long long)b * p.strideC + row;
+                const float bias_row = load_bias(p, row);
                 const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
                 // beta * C: the old values of chunk c+1 are loaded while chunk c
                 // is converted and stored, so C's read latency is paid once per
@@ -499,7 +520,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                             const int col = n0 + c0 + j;
                             if (col < p.n)
                                 store_out<OUT>(p.C, base + (long long)col * p.ldc, v[j], old[j],
-                                               use_beta, alpha, beta, ia, ib);
+                                               use_beta, alpha, beta, ia, ib, p.epi, bias_row);
                         }
                     }
 #pragma unroll
@@ -836,6 +857,9 @@ int gemm_tc(const GemmDesc& d, cudaStream_t s) {
     p.alpha = d.alpha; p.beta = d.beta;
     p.ialpha = d.ialpha; p.ibeta = d.ibeta;
     p.alpha_dev = d.alpha_dev; p.beta_dev = d.beta_dev;
+    p.epi = d.Ctype == kR32I ? 0 : d.epi;
+    p.bias = d.bias;
+    p.bias_type = d.bias_type;
 
     switch (d.kind) {
     case Kind::F16:
