@@ -58,6 +58,8 @@ struct Handle {
     size_t user_ws_bytes = 0;
     void* scratch = nullptr;         // library-owned, grown on demand
     size_t scratch_bytes = 0;
+    void* split_ws = nullptr;        // K-split tail workspace (counters, then partials)
+    unsigned long long split_epoch = 0;
     std::mutex mu;
 };
 
@@ -100,6 +102,39 @@ static cublasStatus_t map_launch(int rc) {
     return CUBLAS_STATUS_EXECUTION_FAILED;
 }
 
+// Workspace of the tensor-core kernel's K-split tail (GemmDesc::split_work):
+// tile counters, then partial sums; the largest split needs 2 * 74 parts of
+// 128 x 256 fp32 values (18.9 MB).  Allocated on the handle's first GEMM,
+// except inside a stream capture, where the GEMM goes without it.  Each
+// launch gets the next epoch.  Called with h->mu held.
+constexpr size_t kSplitCounterBytes = 4096;
+constexpr size_t kSplitWorkBytes = 20u << 20;
+
+static void attach_split_ws(Handle* h, GemmDesc& d, cudaStream_t s) {
+    if (!h->split_ws) {
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        if (cudaStreamIsCapturing(s, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) {
+            cudaGetLastError();
+            return;
+        }
+        void* p = nullptr;
+        if (cudaMalloc(&p, kSplitCounterBytes + kSplitWorkBytes) != cudaSuccess) {
+            cudaGetLastError();
+            return;
+        }
+        if (cudaMemsetAsync(p, 0, kSplitCounterBytes, s) != cudaSuccess) {
+            cudaGetLastError();
+            cudaFree(p);
+            return;
+        }
+        h->split_ws = p;
+    }
+    d.split_counters = static_cast<unsigned long long*>(h->split_ws);
+    d.split_work = reinterpret_cast<uint32_t*>(static_cast<char*>(h->split_ws) + kSplitCounterBytes);
+    d.split_work_bytes = kSplitWorkBytes;
+    d.split_epoch = ++h->split_epoch;
+}
+
 // Runs one validated GEMM description: tensor cores first, CUDA cores when
 // the layout is outside what TMA can describe.
 static cublasStatus_t run_gemm(Handle* h, GemmDesc& d, cudaStream_t s) {
@@ -139,10 +174,13 @@ static cublasStatus_t run_gemm(Handle* h, GemmDesc& d, cudaStream_t s) {
         e.strideA = (long long)d.m * kp;
         e.strideB = (long long)d.n * kp;
         e.A_hi = a_hi; e.A_lo = a_lo; e.B_hi = b_hi; e.B_lo = b_lo;
+        attach_split_ws(h, e, s);
         rc = gemm_tc(e, s);
         if (rc == 1) rc = gemm_simt(d, s);   // plain fp32 on CUDA cores
         return map_launch(rc);
     }
+    std::lock_guard<std::mutex> lock(h->mu);
+    attach_split_ws(h, d, s);
     int rc = gemm_tc(d, s);
     if (rc == 1) rc = gemm_simt(d, s);
     return map_launch(rc);
@@ -261,11 +299,12 @@ cublasStatus_t cublasCreate_v2(cublasHandle_t* handle) {
 cublasStatus_t cublasDestroy_v2(cublasHandle_t handle) {
     Handle* h = as_handle(handle);
     if (!h) return CUBLAS_STATUS_NOT_INITIALIZED;
-    if (h->scratch) {
+    if (h->scratch || h->split_ws) {
         int cur = 0;
         cudaGetDevice(&cur);
         cudaSetDevice(h->device);
-        cudaFree(h->scratch);
+        if (h->scratch) cudaFree(h->scratch);
+        if (h->split_ws) cudaFree(h->split_ws);
         cudaSetDevice(cur);
     }
     h->magic = 0;

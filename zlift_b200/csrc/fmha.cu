@@ -15,8 +15,11 @@
 //               running max grew by more than 2^8 (lazy rescaling: the
 //               final O / l uses the same stale max, so the result is
 //               exact), and at the end normalise O and store it with LSE.
-//   warp 8      TMA producer: Q tiles once, then K and V tiles into a
-//               two-stage ring.
+//   warp 8      TMA producer: Q tiles once, then K_0, V_0, K_1, V_1, ...
+//               through a ring of NSLOT tile slots, each released by the
+//               MMA issuer as soon as its last reader has run (K_j after
+//               the second tile's Q.K_j^T, V_j after its P.V_j), so loads
+//               run well over a key step ahead.
 //   warp 9      MMA issuer (one thread): S_t = Q_t.K_j^T (both operands in
 //               shared memory) and O_t += P_t.V_j (P from TMEM, V in shared
 //               memory), alternating the two query tiles so that one
@@ -47,10 +50,13 @@ struct FCfg {
     static constexpr int BOXES = D / 64;                 // 128-byte column boxes per row
     static constexpr int TILE_BYTES = 128 * D * 2;       // one Q, K or V tile
     static constexpr int Q_OFF = 0;                      // two Q tiles
-    static constexpr int KV_OFF = 2 * TILE_BYTES;        // stage s: K at +2s*TILE, V after
-    static constexpr int STAGES = 2;
-    static constexpr int BAR_OFF = KV_OFF + STAGES * 2 * TILE_BYTES;
+    static constexpr int KV_OFF = 2 * TILE_BYTES;        // K/V ring: slot s at +s*TILE
+    static constexpr int SLOTS_FIT = (227 * 1024 - 1280 - KV_OFF) / TILE_BYTES;
+    static constexpr int NSLOT = SLOTS_FIT > 8 ? 8 : SLOTS_FIT;
+    static constexpr int BAR_OFF = KV_OFF + NSLOT * TILE_BYTES;
     static constexpr int SMEM = BAR_OFF + 256 + 1024;
+    static_assert(NSLOT >= 4, "K/V ring too shallow");
+    static_assert(SMEM <= 227 * 1024, "shared memory");
     static constexpr uint32_t S_COL0 = 0, S_COL1 = 128;
     static constexpr uint32_t O_COL0 = 256, O_COL1 = 256 + D;
     static constexpr uint32_t TMEM_COLS = 512;
@@ -131,16 +137,16 @@ fmha_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    constexpr int NSLOT = C::NSLOT;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
     uint64_t* qfull = bars + 0;
-    uint64_t* kfull = bars + 1;       // [2]
-    uint64_t* vfull = bars + 3;       // [2]
-    uint64_t* kvempty = bars + 5;     // [2]
-    uint64_t* sfull = bars + 7;       // [2] per query tile
-    uint64_t* pready = bars + 9;      // [2]
-    uint64_t* ofinal = bars + 11;     // [2]
-    uint64_t* phalf = bars + 13;      // [2] first half of P (keys 0-63) stored
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
+    uint64_t* sfull = bars + 1;       // [2] per query tile
+    uint64_t* pready = bars + 3;      // [2]
+    uint64_t* ofinal = bars + 5;      // [2]
+    uint64_t* phalf = bars + 7;       // [2] first half of P (keys 0-63) stored
+    uint64_t* kvfull = bars + 9;      // [NSLOT] ring slot loaded
+    uint64_t* kvempty = kvfull + NSLOT;   // [NSLOT] ring slot released
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(kvempty + NSLOT);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -160,10 +166,11 @@ fmha_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
 
     if (threadIdx.x == 0) {
         mbar_init(qfull, 1);
-        for (int i = 0; i < 2; i++) {
-            mbar_init(&kfull[i], 1);
-            mbar_init(&vfull[i], 1);
+        for (int i = 0; i < NSLOT; i++) {
+            mbar_init(&kvfull[i], 1);
             mbar_init(&kvempty[i], 1);
+        }
+        for (int i = 0; i < 2; i++) {
             mbar_init(&sfull[i], 1);
             mbar_init(&pready[i], 4);
             mbar_init(&phalf[i], 4);
@@ -192,18 +199,27 @@ fmha_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
                 for (int x = 0; x < C::BOXES; x++)
                     tma_load_4d(smem + C::Q_OFF + t * C::TILE_BYTES + x * BOX_BYTES, &tmQ, qfull,
                                 x * 64, t ? q01 : q00, h, b);
-            for (int j = 0; j < nmax; j++) {
-                const int st = j & 1;
-                if (!mbar_wait(&kvempty[st], ((j >> 1) & 1) ^ 1u, abort_flag)) break;
-                uint8_t* kt = smem + C::KV_OFF + st * 2 * C::TILE_BYTES;
-                uint8_t* vt = kt + C::TILE_BYTES;
-                mbar_expect_tx(&kfull[st], C::TILE_BYTES);
+            // item i: K_{i/2} (even i) or V_{i/2} (odd i), in slot i % NSLOT
+            const int items = 2 * nmax;
+            bool ok = true;
+            for (int i = 0; i < items; i++) {
+                const int slot = i % NSLOT;
+                if (!mbar_wait(&kvempty[slot], ((i / NSLOT) & 1) ^ 1u, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                uint8_t* dst = smem + C::KV_OFF + slot * C::TILE_BYTES;
+                mbar_expect_tx(&kvfull[slot], C::TILE_BYTES);
+                const CUtensorMap* tm = (i & 1) ? &tmV : &tmK;
                 for (int x = 0; x < C::BOXES; x++)
-                    tma_load_4d(kt + x * BOX_BYTES, &tmK, &kfull[st], x * 64, j * BKEY, hk, b);
-                mbar_expect_tx(&vfull[st], C::TILE_BYTES);
-                for (int x = 0; x < C::BOXES; x++)
-                    tma_load_4d(vt + x * BOX_BYTES, &tmV, &vfull[st], x * 64, j * BKEY, hk, b);
+                    tma_load_4d(dst + x * BOX_BYTES, tm, &kvfull[slot], x * 64, (i >> 1) * BKEY,
+                                hk, b);
             }
+            // drain: the releases of the last NSLOT items are tcgen05.commit
+            // arrivals on this CTA's barriers; none may still be in flight
+            // when the CTA exits
+            for (int i = items > NSLOT ? items - NSLOT : 0; ok && i < items; i++)
+                ok = mbar_wait(&kvempty[i % NSLOT], (i / NSLOT) & 1, abort_flag);
         }
     } else if (warp == 9) {
         // ---------------- MMA issuer ----------------
@@ -211,8 +227,14 @@ fmha_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
             const uint32_t sq_base = smem_u32(smem + C::Q_OFF);
             const uint32_t scol[2] = {C::S_COL0, C::S_COL1};
             const uint32_t ocol[2] = {C::O_COL0, C::O_COL1};
+            // ring slot and wait parity of K_j (item 2j) and V_j (item 2j+1)
+            auto slot_of = [](int item) { return item % NSLOT; };
+            auto par_of = [](int item) { return (uint32_t)((item / NSLOT) & 1); };
+            auto slot_addr = [&](int item) {
+                return smem_u32(smem + C::KV_OFF + slot_of(item) * C::TILE_BYTES);
+            };
             auto issue_qk = [&](int t, int j) {
-                const uint32_t kb = smem_u32(smem + C::KV_OFF + (j & 1) * 2 * C::TILE_BYTES);
+                const uint32_t kb = slot_addr(2 * j);
                 const uint32_t qb = sq_base + t * C::TILE_BYTES;
 #pragma unroll
                 for (int ks = 0; ks < D / 16; ks++) {
@@ -224,8 +246,7 @@ fmha_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
             };
             // half 0: keys 0-63 of the tile, half 1: keys 64-127
             auto issue_pv = [&](int t, int j, int half) {
-                const uint32_t vb =
-                    smem_u32(smem + C::KV_OFF + (j & 1) * 2 * C::TILE_BYTES + C::TILE_BYTES);
+                const uint32_t vb = slot_addr(2 * j + 1);
 #pragma unroll
                 for (int ks = half * (BKEY / 32); ks < (half + 1) * (BKEY / 32); ks++) {
                     // P: 16 keys = 8 packed TMEM columns per step; V: 16 key rows
@@ -234,22 +255,27 @@ fmha_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
                                (j > 0 || ks > 0) ? 1u : 0u);
                 }
             };
-            bool ok = mbar_wait(qfull, 0, abort_flag) && mbar_wait(&kfull[0], 0, abort_flag);
+            // Each ring item is released by one commit after its last reader:
+            // tile 1 when it needs that key tile, else tile 0 (tile 1 has no
+            // key tiles when its queries start past sq).  The ofinal commits
+            // come after every release, so a CTA whose softmax warps have
+            // seen both ofinal has no commit arrival left in flight but the
+            // ones the producer drains.
+            bool ok = mbar_wait(qfull, 0, abort_flag) && mbar_wait(&kvfull[0], 0, abort_flag);
             if (ok) {
                 tc_fence_after();
                 if (nt0 > 0) issue_qk(0, 0);
                 if (nt1 > 0) issue_qk(1, 0);
+                mma_commit(&kvempty[slot_of(0)]);
             }
             for (int j = 0; ok && j < nmax; j++) {
-                const int st = j & 1;
-                const uint32_t kv_par = (j >> 1) & 1;
-                if (!mbar_wait(&vfull[st], kv_par, abort_flag)) break;
-                const bool next_k = j + 1 < nmax;
+                if (!mbar_wait(&kvfull[slot_of(2 * j + 1)], par_of(2 * j + 1), abort_flag)) break;
                 bool have_next_k = false;
 #pragma unroll
                 for (int t = 0; t < 2; t++) {
                     const int ntt = t ? nt1 : nt0;
                     if (j >= ntt) continue;
+                    const bool last_reader = t == 1 || j >= nt1;
                     // P.V on the first half of P while the softmax finishes the second
                     if (!mbar_wait(&phalf[t], j & 1, abort_flag)) { ok = false; break; }
                     tc_fence_after();
@@ -257,10 +283,12 @@ fmha_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
                     if (!mbar_wait(&pready[t], j & 1, abort_flag)) { ok = false; break; }
                     tc_fence_after();
                     issue_pv(t, j, 1);
+                    if (last_reader) mma_commit(&kvempty[slot_of(2 * j + 1)]);
                     if (j + 1 == ntt) mma_commit(&ofinal[t]);
                     if (j + 1 < ntt) {
                         if (!have_next_k) {
-                            if (!mbar_wait(&kfull[(j + 1) & 1], ((j + 1) >> 1) & 1, abort_flag)) {
+                            if (!mbar_wait(&kvfull[slot_of(2 * j + 2)], par_of(2 * j + 2),
+                                           abort_flag)) {
                                 ok = false;
                                 break;
                             }
@@ -268,10 +296,9 @@ fmha_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
                             have_next_k = true;
                         }
                         issue_qk(t, j + 1);
+                        if (t == 1 || j + 1 >= nt1) mma_commit(&kvempty[slot_of(2 * j + 2)]);
                     }
                 }
-                (void)next_k;
-                mma_commit(&kvempty[st]);
             }
         }
     } else {

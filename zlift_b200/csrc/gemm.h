@@ -51,6 +51,15 @@ struct GemmDesc {
     int epi;
     const void* bias;
     int bias_type;
+    // Workspace for splitting the last wave of tiles along K (null: never
+    // split): split_work_bytes of device memory for partial sums and one
+    // counter per split tile and CTA (at most 2 * number of SMs), zero on
+    // first use.  split_epoch tags the launch (a different value per launch
+    // that shares the workspace, nonzero, < 2^48).
+    uint32_t* split_work = nullptr;
+    size_t split_work_bytes = 0;
+    unsigned long long* split_counters = nullptr;
+    unsigned long long split_epoch = 0;
 };
 
 enum EpiFlags : int { kEpiBias = 1, kEpiRelu = 2, kEpiGelu = 4 };

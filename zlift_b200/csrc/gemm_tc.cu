@@ -17,6 +17,11 @@
 //               alpha*acc + beta*C, convert, store to C.  The two TMEM
 //               accumulators let the epilogue of tile i overlap the main
 //               loop of tile i+1.
+// When the last wave of tiles would leave more than half of the CTAs idle,
+// each of its tiles is split along K into 2-4 parts run by different CTAs
+// (see unit_of and last_part): the parts park their partial sums in a
+// workspace, and the part that finishes last adds them up in part order and
+// runs the epilogue.
 // Column-major operands need no staging transpose (the reference's
 // stage_tight, zblas_gpu.cpp:633-669): an operand whose contiguous
 // dimension is M or N is described to the tensor core as "MN-major".
@@ -61,7 +66,86 @@ struct TcParams {
     int epi;                 // EpiFlags (floating-point outputs)
     const void* bias;
     int bias_type;
+    // Units of work: units [0, main_units) are whole tiles (unit u = tile
+    // u); each later tile is split along K into `split` units.  split == 1:
+    // main_units = total_units = number of tiles.
+    int main_units, total_units, split;
+    uint32_t* work;                  // partial sums of split tiles (fp32 or int32 bits)
+    size_t work_bytes;
+    unsigned long long* counters;    // per (split tile, CTA rank): epoch << 16 | parts done
+    unsigned long long epoch;        // this launch's tag, < 2^48
 };
+
+// What one unit of work covers: output tile `t` and K blocks [kb0, kb1);
+// part >= 0 for a K-split unit.
+struct Unit {
+    int t, kb0, kb1, part;
+};
+
+__device__ __forceinline__ Unit unit_of(const TcParams& p, int u) {
+    Unit r;
+    if (u < p.main_units) {
+        r.t = u;
+        r.kb0 = 0;
+        r.kb1 = p.k_blocks;
+        r.part = -1;
+    } else {
+        const int v = u - p.main_units;
+        const int s = v % p.split;
+        r.t = p.main_units + v / p.split;
+        r.part = s;
+        r.kb0 = (int)((long long)s * p.k_blocks / p.split);
+        r.kb1 = (int)((long long)(s + 1) * p.k_blocks / p.split);
+    }
+    return r;
+}
+
+// Counts one finished part of split tile `tt` (this CTA's rows); true for
+// the part that completes the tile.  The counter carries the launch's epoch
+// so a count left by an aborted launch reads as zero; the last part resets
+// it, so a CUDA graph replaying this launch with the same epoch starts from
+// zero too.  No CTA ever waits for another.
+__device__ __forceinline__ bool last_part(const TcParams& p, int slot) {
+    unsigned long long* c = p.counters + slot;
+    unsigned long long cur = atomicAdd(c, 0ull);
+    while (true) {
+        const unsigned long long done = (cur >> 16) == p.epoch ? (cur & 0xffffull) : 0ull;
+        const unsigned long long next = (p.epoch << 16) | (done + 1);
+        const unsigned long long prev = atomicCAS(c, cur, next);
+        if (prev == cur) {
+            if (done + 1 < (unsigned long long)p.split) return false;
+            atomicExch(c, 0ull);
+            return true;
+        }
+        cur = prev;
+    }
+}
+
+// Sum over the parts of a split tile, in part order, for this thread's row
+// and 32 columns: part `own` is v (this CTA's accumulator); the others come
+// from `staged`, their 32 x 128 chunks one after another in part order.
+// Part order makes the bits independent of which part completed the tile.
+template <int OUT>
+__device__ __forceinline__ void combine_parts(uint32_t (&v)[32], const uint32_t* staged,
+                                              int split, int own, int row) {
+#pragma unroll
+    for (int j = 0; j < 32; j++) {
+        uint32_t acc = 0;
+        int other = 0;
+        for (int q = 0; q < split; q++) {
+            uint32_t x;
+            if (q == own) {
+                x = v[j];
+            } else {
+                x = staged[(size_t)other * 32 * BM + j * BM + row];
+                other++;
+            }
+            if constexpr (OUT == kR32I) acc = q ? acc + x : x;
+            else acc = q ? __float_as_uint(__uint_as_float(acc) + __uint_as_float(x)) : x;
+        }
+        v[j] = acc;
+    }
+}
 
 // bias[row] as float (0 past the end or without a bias)
 __device__ __forceinline__ float load_bias(const TcParams& p, long long row) {
@@ -239,8 +323,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
     uint64_t* tfull = empty + STAGES;
     uint64_t* tempty = tfull + 2;
     uint64_t* cbar = tempty + 2;                          // C chunk loaded, per buffer
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(cbar + 2);
+    uint64_t* rbar = cbar + 2;                            // split partials staged, per ring slot
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rbar + 3);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    volatile int* split_last = abort_flag + 1;            // epilogue: this part completes its tile
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // CTA pair: rank 0 (leader) issues the MMAs for both; each CTA loads its
@@ -259,6 +345,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
             mbar_init(&tempty[a], PAIR ? 8 : 4);   // one arrival per epilogue warp (of both CTAs)
             mbar_init(&cbar[a], 1);
         }
+        for (int a = 0; a < 3; a++) mbar_init(&rbar[a], 1);
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -286,19 +373,20 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
-    const int total = p.tiles_m * p.tiles_n * p.batch;
+    const int total = p.total_units;
 
     if (warp == 0) {
         // ---------------- TMA producer ----------------
         if (lane == 0) {
             int stage = 0;
             uint32_t phase = 0;
-            for (int t = cta_id; t < total; t += n_ctas) {
+            for (int u = cta_id; u < total; u += n_ctas) {
+                const Unit un = unit_of(p, u);
                 int b, tm, tn;
-                decode_tile(t, p.tiles_m, p.tiles_n, b, tm, tn);
+                decode_tile(un.t, p.tiles_m, p.tiles_n, b, tm, tn);
                 const int m0 = tm * TILE_M + (int)rank * BM;
                 const int n0 = tn * BN + (int)rank * B_ROWS;
-                for (int kb = 0; kb < p.k_blocks; kb++) {
+                for (int kb = un.kb0; kb < un.kb1; kb++) {
                     if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) goto producer_done;
                     uint8_t* sa = smem + stage * STAGE_BYTES;
                     uint8_t* sb = sa + A_BYTES;
@@ -337,13 +425,14 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
             int stage = 0;
             uint32_t phase = 0;
             int local = 0;
-            for (int t = cta_id; t < total; t += n_ctas, local++) {
+            for (int u = cta_id; u < total; u += n_ctas, local++) {
+                const Unit un = unit_of(p, u);
                 const int acc = local & 1;
                 const uint32_t aphase = (local >> 1) & 1;
                 if (!mbar_wait(&tempty[acc], aphase ^ 1u, abort_flag)) break;
                 tc_fence_after();
                 const uint32_t d = tmem_base + acc * BN;
-                for (int kb = 0; kb < p.k_blocks; kb++) {
+                for (int kb = un.kb0; kb < un.kb1; kb++) {
                     if (!mbar_wait(&full[stage], phase, abort_flag)) goto mma_done;
                     tc_fence_after();
                     const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
@@ -352,7 +441,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                     for (int ks = 0; ks < KSTEPS; ks++) {
                         const uint64_t ad = operand_desc<A_MN, BK, UK>(sa, ks);
                         const uint64_t bd = operand_desc<B_MN, BK, UK>(sb, ks);
-                        const uint32_t accum = (kb | ks) != 0 ? 1u : 0u;
+                        const uint32_t accum = (kb != un.kb0 || ks != 0) ? 1u : 0u;
                         if constexpr (KIND == (int)Kind::TF32X3) {
                             // small terms first: lo*hi, hi*lo, then hi*hi
                             const uint64_t ad2 = operand_desc<A_MN, BK, UK>(sb + B_BYTES, ks);
@@ -407,21 +496,77 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
             const int et = threadIdx.x - 64;           // 0..127
             const bool leader = et == 0;
             uint32_t cphase = 0;                       // bit i: parity of cbar[i]
+            uint32_t rphase = 0;                       // bit i: parity of rbar[i]
             int chunk = 0;
             int local = 0;
             bool ok = true;
-            for (int t = cta_id; ok && t < total; t += n_ctas, local++) {
+            for (int u = cta_id; ok && u < total; u += n_ctas, local++) {
+                const Unit un = unit_of(p, u);
                 const int acc = local & 1;
                 const uint32_t aphase = (local >> 1) & 1;
                 ok = named_bar_and(1, 128, mbar_wait(&tfull[acc], aphase, abort_flag));
                 if (!ok) break;
                 tc_fence_after();
                 int b, tm, tn;
-                decode_tile(t, p.tiles_m, p.tiles_n, b, tm, tn);
+                decode_tile(un.t, p.tiles_m, p.tiles_n, b, tm, tn);
                 const int m0 = tm * TILE_M + (int)rank * BM, n0 = tn * BN;
                 const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
                 const int ncols = min(BN, p.n - n0);
                 const float bias_row = load_bias(p, (long long)m0 + r_in_tile);
+                // K-split unit: store this part's partial sums ([column][row]
+                // of this CTA's 128 rows), count the part, and go on only if
+                // it completed the tile.  That part adds the other parts'
+                // sums, which it copies chunk by chunk (32 columns, 16 KB per
+                // part) into the operand ring, idle by now: a split unit is
+                // its CTA's last.  Up to `rslots` chunks are in flight.
+                constexpr int RANKS = PAIR ? 2 : 1;
+                constexpr uint32_t kChunkBytes = 32 * BM * 4;
+                const size_t tile_words = (size_t)BN * BM;
+                int own = -1;                          // >= 0: completing part
+                const uint32_t* part0 = nullptr;       // part 0's sums, this CTA's rows
+                int rslots = 0;
+                auto fetch = [&](int c) {              // leader: chunk c of the other parts
+                    const int sl = c % rslots;
+                    uint8_t* dst = smem + (size_t)sl * (p.split - 1) * kChunkBytes;
+                    mbar_expect_tx(&rbar[sl], (uint32_t)(p.split - 1) * kChunkBytes);
+                    for (int q = 0, i = 0; q < p.split; q++) {
+                        if (q == own) continue;
+                        bulk_load(dst + (size_t)i * kChunkBytes,
+                                  part0 + (size_t)q * RANKS * tile_words + (size_t)c * 32 * BM,
+                                  kChunkBytes, &rbar[sl]);
+                        i++;
+                    }
+                };
+                if (un.part >= 0) {
+                    const int tt = un.t - p.main_units;
+                    uint32_t* mine =
+                        p.work + (((size_t)tt * p.split + un.part) * RANKS + rank) * tile_words;
+#pragma unroll 1
+                    for (int c0 = 0; c0 < ncols; c0 += 32) {
+                        uint32_t v[32];
+                        tmem_ld32(taddr + c0, v);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int j = 0; j < 32; j++)
+                            __stcg(mine + (size_t)(c0 + j) * BM + r_in_tile, v[j]);
+                    }
+                    __threadfence();
+                    named_bar_sync(1, 128);
+                    if (leader) *split_last = last_part(p, tt * RANKS + (int)rank) ? 1 : 0;
+                    named_bar_sync(1, 128);
+                    if (!*split_last) {
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) release_acc(&tempty[acc], rank);
+                        continue;
+                    }
+                    __threadfence();
+                    own = un.part;
+                    part0 = p.work + ((size_t)tt * p.split * RANKS + rank) * tile_words;
+                    rslots = max(1, min(3, (STAGES * STAGE_BYTES) / ((p.split - 1) * (int)kChunkBytes)));
+                    if (leader)
+                        for (int c = 0; c < rslots && c * 32 < ncols; c++) fetch(c);
+                }
 #pragma unroll 1
                 for (int c0 = 0; c0 < ncols; c0 += kEpiCols, chunk++) {
                     const int buf = chunk & 1;
@@ -440,9 +585,19 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                         w = mbar_wait(&cbar[buf], (cphase >> buf) & 1u, abort_flag);
                         cphase ^= 1u << buf;
                     }
+                    const int sl = own >= 0 ? (c0 / 32) % rslots : 0;
+                    if (own >= 0) {
+                        w = mbar_wait(&rbar[sl], (rphase >> sl) & 1u, abort_flag) && w;
+                        rphase ^= 1u << sl;
+                    }
                     tmem_wait_ld();
                     ok = named_bar_and(1, 128, w);
                     if (!ok) break;
+                    if (own >= 0)
+                        combine_parts<OUT>(v,
+                                           reinterpret_cast<const uint32_t*>(
+                                               smem + (size_t)sl * (p.split - 1) * kChunkBytes),
+                                           p.split, own, r_in_tile);
 #pragma unroll
                     for (int j = 0; j < 32; j++) {
                         uint8_t* e = sbuf + (j * BM + r_in_tile) * ES;
@@ -473,6 +628,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                     if (leader) {
                         tma_store_3d(&tmC, sbuf, m0, n0 + c0, b);
                         bulk_commit();
+                        // every thread has read ring slot sl: refill it
+                        if (own >= 0 && c0 + 32 * rslots < ncols) fetch(c0 / 32 + rslots);
                     }
                 }
                 tc_fence_before();
@@ -482,13 +639,14 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
             if (leader) bulk_wait<0>();
         } else {
             int local = 0;
-            for (int t = cta_id; t < total; t += n_ctas, local++) {
+            // (the host never splits K for this epilogue: every unit is a tile)
+            for (int u = cta_id; u < total; u += n_ctas, local++) {
                 const int acc = local & 1;
                 const uint32_t aphase = (local >> 1) & 1;
                 if (!mbar_wait(&tfull[acc], aphase, abort_flag)) break;
                 tc_fence_after();
                 int b, tm, tn;
-                decode_tile(t, p.tiles_m, p.tiles_n, b, tm, tn);
+                decode_tile(unit_of(p, u).t, p.tiles_m, p.tiles_n, b, tm, tn);
                 const long long row = (long long)tm * TILE_M + (int)rank * BM + r_in_tile;
                 const bool row_ok = row < p.m;
                 const int n0 = tn * BN;
@@ -645,6 +803,33 @@ constexpr bool pair_ok(int kind, int bn) {
            ((bn == 256 || bn == 128) && (kind == (int)Kind::F16 || kind == (int)Kind::BF16));
 }
 
+// K split of the last wave.  `tiles` tiles on `slots` persistent CTAs (or
+// pairs) leave the last wave R = tiles % slots tiles; when R is at most half
+// of the slots, each of those tiles is split into S = min(slots / R, 4)
+// parts along K (each part at least 4 K blocks), so the last wave takes
+// about 1/S of a tile's time.  `unit_bytes` is the workspace one part of
+// one tile needs (0: this configuration does not split).  The part that
+// completes a tile stages the other S-1 parts' 16 KB column chunks in the
+// operand ring (`ring_bytes`), so S-1 chunks must fit there.  Without a
+// workspace large enough, nothing is split.
+void split_tail(TcParams& q, int tiles, int slots, size_t unit_bytes, size_t ring_bytes) {
+    q.main_units = q.total_units = tiles;
+    q.split = 1;
+    const char* on = getenv("ZBLAS_SPLIT_K");           // opt-in for now
+    if (!on || on[0] == '0') return;
+    if (!q.work || !q.counters || unit_bytes == 0 || slots <= 1) return;
+    const int rem = tiles % slots;
+    if (rem == 0 || 2 * rem > slots) return;
+    int parts = slots / rem;
+    if (parts > 4) parts = 4;
+    while (parts > 1 && (q.k_blocks / parts < 4 || (size_t)(parts - 1) * 32 * BM * 4 > ring_bytes))
+        parts--;
+    if (parts < 2 || (size_t)rem * parts * unit_bytes > q.work_bytes) return;
+    q.split = parts;
+    q.main_units = tiles - rem;
+    q.total_units = q.main_units + rem * parts;
+}
+
 template <int KIND, int BN, bool A_MN, bool B_MN, int OUT, bool EPI_TMA, bool PAIR>
 int launch_one(const Maps& m, const TcParams& p, cudaStream_t s) {
     using C_ = Cfg<BN, KIND, EPI_TMA ? out_es(OUT) : 0, PAIR>;
@@ -681,10 +866,15 @@ int launch_one(const Maps& m, const TcParams& p, cudaStream_t s) {
         }
         attr_set.fetch_or(bit);
     }
-    const int total = p.tiles_m * p.tiles_n * p.batch;
+    const int slots = PAIR ? (max_clusters[dev & 63] > 0 ? max_clusters[dev & 63] : num_sms() / 2)
+                           : num_sms();
+    TcParams q = p;
+    const int tiles = p.tiles_m * p.tiles_n * p.batch;
+    split_tail(q, tiles, slots, m.staged ? BN * BM * 4 * (PAIR ? 2 : 1) : 0,
+               (size_t)C_::STAGES * C_::STAGE_BYTES);
+    const int total = q.total_units;
     cudaError_t e;
     if constexpr (PAIR) {
-        const int slots = max_clusters[dev & 63] > 0 ? max_clusters[dev & 63] : num_sms() / 2;
         const int clusters = total < slots ? total : slots;
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(2 * clusters);
@@ -698,10 +888,10 @@ int launch_one(const Maps& m, const TcParams& p, cudaStream_t s) {
         attr[0].val.clusterDim.z = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        e = cudaLaunchKernelEx(&cfg, kern, m.a, m.b, m.a2, m.b2, m.c, p);
+        e = cudaLaunchKernelEx(&cfg, kern, m.a, m.b, m.a2, m.b2, m.c, q);
     } else {
-        const int grid = total < num_sms() ? total : num_sms();
-        kern<<<grid, kThreads, C_::SMEM, s>>>(m.a, m.b, m.a2, m.b2, m.c, p);
+        const int grid = total < slots ? total : slots;
+        kern<<<grid, kThreads, C_::SMEM, s>>>(m.a, m.b, m.a2, m.b2, m.c, q);
         e = cudaGetLastError();
     }
     if (e == cudaSuccess) note_launch();
@@ -860,6 +1050,12 @@ int gemm_tc(const GemmDesc& d, cudaStream_t s) {
     p.epi = d.Ctype == kR32I ? 0 : d.epi;
     p.bias = d.bias;
     p.bias_type = d.bias_type;
+    p.work = d.split_work;
+    p.work_bytes = d.split_work_bytes;
+    p.counters = d.split_counters;
+    p.epoch = d.split_epoch & 0xffffffffffffull;
+    p.main_units = p.total_units = p.tiles_m * p.tiles_n * p.batch;
+    p.split = 1;
 
     switch (d.kind) {
     case Kind::F16:

@@ -147,6 +147,17 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap* m, const void* s
         : "memory");
 }
 
+// global -> shared linear copy of `bytes` (a multiple of 16; both addresses
+// 16-byte aligned), completing as transaction bytes on `bar` (no multicast)
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+        :: "r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes),
+           "r"(smem_u32(bar))
+        : "memory");
+}
+
 __device__ __forceinline__ void bulk_commit() {
     asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
