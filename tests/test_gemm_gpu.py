@@ -285,3 +285,25 @@ def test_pair_tiles_strided_batched(handle, oracle_lib):
                                           k * n, 0.0, dC, 14, m, m * n, batch) == 0
     got = as_float(from_dev(dC, "bf16"), "bf16")
     assert normwise(got, as_float(cref, "bf16")) <= 1e-2
+
+
+@pytest.mark.parametrize("k", [1024, 4096, 16384])
+def test_sgemm_long_k_accuracy(handle, oracle_lib, k):
+    """fp32 GEMM accuracy does not decay with K: the 3xTF32 kernel adds
+    128-deep accumulator chunks in fp32 (round to nearest), so the error
+    against an fp64 product of the same inputs stays near 1e-6 where one
+    tensor-core accumulation over K reached 1.2e-4 at K = 16384."""
+    from zlift_b200 import inputs
+    m = n = 256
+    A = inputs.make("f32", "uniform", 61, m * k)
+    B = inputs.make("f32", "uniform", 62, k * n)
+    exact = (A.astype(np.float64).reshape(k, m).T @ B.astype(np.float64).reshape(n, k).T)
+    exact = exact.T.reshape(-1)
+    cref = np.zeros(m * n, np.float32)
+    assert oracle_lib.gemm_ex(0, 0, m, n, k, 1.0, A, 0, m, B, 0, k, 0.0, cref, 0, m) == 0
+    dA, dB = to_dev(A, "f32"), to_dev(B, "f32")
+    dC = to_dev(np.zeros(m * n, np.float32), "f32")
+    assert handle.sgemm(0, 0, m, n, k, 1.0, dA, m, dB, k, 0.0, dC, m) == 0
+    got = from_dev(dC, "f32").astype(np.float64)
+    assert normwise(got, exact) <= 2e-6
+    assert normwise(got, cref.astype(np.float64)) <= 1e-5

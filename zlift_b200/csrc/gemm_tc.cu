@@ -70,6 +70,7 @@ struct TcParams {
     // u); each later tile is split along K into `split` units.  split == 1:
     // main_units = total_units = number of tiles.
     int main_units, total_units, split;
+    int kc;                          // K blocks per accumulation chunk (see fold_chunks)
     uint32_t* work;                  // partial sums of split tiles (fp32 or int32 bits)
     size_t work_bytes;
     unsigned long long* counters;    // per (split tile, CTA rank): epoch << 16 | parts done
@@ -121,30 +122,75 @@ __device__ __forceinline__ bool last_part(const TcParams& p, int slot) {
     }
 }
 
-// Sum over the parts of a split tile, in part order, for this thread's row
-// and 32 columns: part `own` is v (this CTA's accumulator); the others come
-// from `staged`, their 32 x 128 chunks one after another in part order.
-// Part order makes the bits independent of which part completed the tile.
+// Sum over the parts of a split tile (2 to 4), in part order, for this
+// thread's row and 32 columns: part `own` is v (this CTA's accumulator);
+// the others come from `staged`, their 32 x 128 chunks one after another
+// in part order with `own` left out.  Part order makes the bits independent
+// of which part completed the tile.  Fully unrolled over 4 parts with
+// predicates, so v stays in registers.
 template <int OUT>
 __device__ __forceinline__ void combine_parts(uint32_t (&v)[32], const uint32_t* staged,
                                               int split, int own, int row) {
+    const uint32_t* src_q[4];
+#pragma unroll
+    for (int q = 0; q < 4; q++)
+        src_q[q] = staged + (size_t)(q < own ? q : q - 1) * 32 * BM + row;
 #pragma unroll
     for (int j = 0; j < 32; j++) {
-        uint32_t acc = 0;
-        int other = 0;
-        for (int q = 0; q < split; q++) {
-            uint32_t x;
-            if (q == own) {
-                x = v[j];
-            } else {
-                x = staged[(size_t)other * 32 * BM + j * BM + row];
-                other++;
-            }
-            if constexpr (OUT == kR32I) acc = q ? acc + x : x;
-            else acc = q ? __float_as_uint(__uint_as_float(acc) + __uint_as_float(x)) : x;
+        uint32_t t[4];
+#pragma unroll
+        for (int q = 0; q < 4; q++)
+            t[q] = q == own ? v[j] : (q < split ? src_q[q][j * BM] : 0u);
+        if constexpr (OUT == kR32I) {
+            uint32_t a = t[0] + t[1];
+            if (split > 2) a += t[2];
+            if (split > 3) a += t[3];
+            v[j] = a;
+        } else {
+            float a = __uint_as_float(t[0]) + __uint_as_float(t[1]);
+            if (split > 2) a += __uint_as_float(t[2]);
+            if (split > 3) a += __uint_as_float(t[3]);
+            v[j] = __float_as_uint(a);
         }
-        v[j] = acc;
     }
+}
+
+// Chunked accumulation (the 3xTF32 kernel): the tensor core's fp32
+// accumulation of tf32 products loses precision at every step, so the error
+// of one long accumulation grows with K.  The MMA issuer starts a fresh
+// accumulator every kc K blocks; the epilogue adds the chunks up in fp32
+// registers, round to nearest, in K order: fold_chunk for every chunk but a
+// unit's last, add_run into the last chunk's TMEM columns.
+template <int BN>
+__device__ __forceinline__ void fold_chunk(uint32_t taddr, float (&run)[BN], bool first) {
+#pragma unroll
+    for (int i = 0; i < BN / 32; i++) {
+        uint32_t v[32];
+        tmem_ld32(taddr + i * 32, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 32; j++)
+            run[i * 32 + j] = first ? __uint_as_float(v[j]) : run[i * 32 + j] + __uint_as_float(v[j]);
+    }
+}
+
+template <int BN>
+__device__ __forceinline__ void add_run(uint32_t taddr, const float (&run)[BN]) {
+#pragma unroll
+    for (int i = 0; i < BN / 32; i++) {
+        uint32_t v[32];
+        tmem_ld32(taddr + i * 32, v);
+        tmem_wait_ld();
+        uint32_t lo[16], hi[16];
+#pragma unroll
+        for (int j = 0; j < 16; j++) {
+            lo[j] = __float_as_uint(run[i * 32 + j] + __uint_as_float(v[j]));
+            hi[j] = __float_as_uint(run[i * 32 + 16 + j] + __uint_as_float(v[16 + j]));
+        }
+        tmem_st16(taddr + i * 32, lo);
+        tmem_st16(taddr + i * 32 + 16, hi);
+    }
+    tmem_wait_st();
 }
 
 // bias[row] as float (0 past the end or without a bias)
@@ -313,6 +359,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
     constexpr uint32_t IDESC =
         make_idesc(KT<KIND>::cfmt, KT<KIND>::abfmt, A_MN ? 1 : 0, B_MN ? 1 : 0, TILE_M, BN);
     constexpr uint32_t TMEM_COLS = C_::TMEM_COLS;
+    constexpr bool CHUNKED = KIND == (int)Kind::TF32X3;
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -425,14 +472,18 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
             int stage = 0;
             uint32_t phase = 0;
             int local = 0;
-            for (int u = cta_id; u < total; u += n_ctas, local++) {
+            // one accumulator per chunk of kc K blocks (a unit is one chunk
+            // unless the kernel accumulates in chunks)
+            for (int u = cta_id; u < total; u += n_ctas) {
                 const Unit un = unit_of(p, u);
+                for (int c0 = un.kb0; c0 < un.kb1; c0 += p.kc, local++) {
+                const int c1 = min(c0 + p.kc, un.kb1);
                 const int acc = local & 1;
                 const uint32_t aphase = (local >> 1) & 1;
-                if (!mbar_wait(&tempty[acc], aphase ^ 1u, abort_flag)) break;
+                if (!mbar_wait(&tempty[acc], aphase ^ 1u, abort_flag)) goto mma_done;
                 tc_fence_after();
                 const uint32_t d = tmem_base + acc * BN;
-                for (int kb = un.kb0; kb < un.kb1; kb++) {
+                for (int kb = c0; kb < c1; kb++) {
                     if (!mbar_wait(&full[stage], phase, abort_flag)) goto mma_done;
                     tc_fence_after();
                     const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
@@ -441,7 +492,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                     for (int ks = 0; ks < KSTEPS; ks++) {
                         const uint64_t ad = operand_desc<A_MN, BK, UK>(sa, ks);
                         const uint64_t bd = operand_desc<B_MN, BK, UK>(sb, ks);
-                        const uint32_t accum = (kb != un.kb0 || ks != 0) ? 1u : 0u;
+                        const uint32_t accum = (kb != c0 || ks != 0) ? 1u : 0u;
                         if constexpr (KIND == (int)Kind::TF32X3) {
                             // small terms first: lo*hi, hi*lo, then hi*hi
                             const uint64_t ad2 = operand_desc<A_MN, BK, UK>(sb + B_BYTES, ks);
@@ -465,6 +516,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                 }
                 if constexpr (PAIR) mma_commit_pair(&tfull[acc], 0x3);
                 else mma_commit(&tfull[acc]);
+                }
             }
         mma_done:;
         }
@@ -502,11 +554,31 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
             bool ok = true;
             for (int u = cta_id; ok && u < total; u += n_ctas, local++) {
                 const Unit un = unit_of(p, u);
+                float run[CHUNKED ? BN : 1];
+                const int nch = CHUNKED ? (un.kb1 - un.kb0 + p.kc - 1) / p.kc : 1;
+                if constexpr (CHUNKED) {
+                    for (int c = 0; c + 1 < nch; c++, local++) {
+                        const int ca = local & 1;
+                        ok = named_bar_and(1, 128,
+                                           mbar_wait(&tfull[ca], (local >> 1) & 1, abort_flag));
+                        if (!ok) break;
+                        tc_fence_after();
+                        fold_chunk<BN>(tmem_base + ((uint32_t)(q * 32) << 16) + ca * BN, run,
+                                       c == 0);
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) release_acc(&tempty[ca], rank);
+                    }
+                    if (!ok) break;
+                }
                 const int acc = local & 1;
                 const uint32_t aphase = (local >> 1) & 1;
                 ok = named_bar_and(1, 128, mbar_wait(&tfull[acc], aphase, abort_flag));
                 if (!ok) break;
                 tc_fence_after();
+                if constexpr (CHUNKED) {
+                    if (nch > 1) add_run<BN>(tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN, run);
+                }
                 int b, tm, tn;
                 decode_tile(un.t, p.tiles_m, p.tiles_n, b, tm, tn);
                 const int m0 = tm * TILE_M + (int)rank * BM, n0 = tn * BN;
@@ -641,12 +713,32 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
             int local = 0;
             // (the host never splits K for this epilogue: every unit is a tile)
             for (int u = cta_id; u < total; u += n_ctas, local++) {
+                const Unit un = unit_of(p, u);
+                float run[CHUNKED ? BN : 1];
+                const int nch = CHUNKED ? (un.kb1 - un.kb0 + p.kc - 1) / p.kc : 1;
+                bool fine = true;
+                if constexpr (CHUNKED) {
+                    for (int c = 0; c + 1 < nch; c++, local++) {
+                        const int ca = local & 1;
+                        if (!mbar_wait(&tfull[ca], (local >> 1) & 1, abort_flag)) { fine = false; break; }
+                        tc_fence_after();
+                        fold_chunk<BN>(tmem_base + ((uint32_t)(q * 32) << 16) + ca * BN, run,
+                                       c == 0);
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) release_acc(&tempty[ca], rank);
+                    }
+                }
+                if (!fine) break;
                 const int acc = local & 1;
                 const uint32_t aphase = (local >> 1) & 1;
                 if (!mbar_wait(&tfull[acc], aphase, abort_flag)) break;
                 tc_fence_after();
+                if constexpr (CHUNKED) {
+                    if (nch > 1) add_run<BN>(tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN, run);
+                }
                 int b, tm, tn;
-                decode_tile(unit_of(p, u).t, p.tiles_m, p.tiles_n, b, tm, tn);
+                decode_tile(un.t, p.tiles_m, p.tiles_n, b, tm, tn);
                 const long long row = (long long)tm * TILE_M + (int)rank * BM + r_in_tile;
                 const bool row_ok = row < p.m;
                 const int n0 = tn * BN;
@@ -1056,6 +1148,8 @@ int gemm_tc(const GemmDesc& d, cudaStream_t s) {
     p.epoch = d.split_epoch & 0xffffffffffffull;
     p.main_units = p.total_units = p.tiles_m * p.tiles_n * p.batch;
     p.split = 1;
+    // 3xTF32: a fresh accumulator every 4 K blocks (128 of K)
+    p.kc = d.kind == Kind::TF32X3 ? 4 : (p.k_blocks > 0 ? p.k_blocks : 1);
 
     switch (d.kind) {
     case Kind::F16:
