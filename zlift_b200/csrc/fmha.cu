@@ -71,6 +71,7 @@ struct FParams {
     float* lse;
     float scale, scale_log2;
     int causal, diag;
+    int half_p;                  // P.V starts on the first half of P (see the MMA issuer)
 };
 
 __device__ __forceinline__ float ex2(float x) {
@@ -138,15 +139,21 @@ fmha_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     constexpr int NSLOT = C::NSLOT;
+    // a step's K and V sit in the ring at most NSLOT/2 + 1 steps ahead of
+    // the MMA issuer, so KV_BARS such barriers are reused only after the
+    // issuer has waited on them
+    constexpr int KV_BARS = NSLOT / 2 + 1;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
     uint64_t* qfull = bars + 0;
     uint64_t* sfull = bars + 1;       // [2] per query tile
-    uint64_t* pready = bars + 3;      // [2]
-    uint64_t* ofinal = bars + 5;      // [2]
-    uint64_t* phalf = bars + 7;       // [2] first half of P (keys 0-63) stored
-    uint64_t* kvfull = bars + 9;      // [NSLOT] ring slot loaded
-    uint64_t* kvempty = kvfull + NSLOT;   // [NSLOT] ring slot released
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(kvempty + NSLOT);
+    uint64_t* ofinal = bars + 3;      // [2]
+    uint64_t* kvfull = bars + 5;      // [KV_BARS] K_j and V_j both landed (step j % KV_BARS)
+    uint64_t* kvempty = kvfull + KV_BARS;   // [NSLOT] ring slot released
+    // softmax -> MMA hand-off counts per query tile (4 warps add 1 each per
+    // key tile): first half of P stored, all of P stored
+    uint32_t* phalf = reinterpret_cast<uint32_t*>(kvempty + NSLOT);   // [2]
+    uint32_t* pready = phalf + 2;                                      // [2]
+    uint32_t* tmem_slot = pready + 2;
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -166,15 +173,13 @@ fmha_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
 
     if (threadIdx.x == 0) {
         mbar_init(qfull, 1);
-        for (int i = 0; i < NSLOT; i++) {
-            mbar_init(&kvfull[i], 1);
-            mbar_init(&kvempty[i], 1);
-        }
+        for (int i = 0; i < KV_BARS; i++) mbar_init(&kvfull[i], 1);
+        for (int i = 0; i < NSLOT; i++) mbar_init(&kvempty[i], 1);
         for (int i = 0; i < 2; i++) {
             mbar_init(&sfull[i], 1);
-            mbar_init(&pready[i], 4);
-            mbar_init(&phalf[i], 4);
             mbar_init(&ofinal[i], 1);
+            phalf[i] = 0;
+            pready[i] = 0;
         }
         *abort_flag = 0;
         fence_mbar_init();
@@ -209,11 +214,11 @@ fmha_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
                     break;
                 }
                 uint8_t* dst = smem + C::KV_OFF + slot * C::TILE_BYTES;
-                mbar_expect_tx(&kvfull[slot], C::TILE_BYTES);
+                uint64_t* full = &kvfull[(i >> 1) % KV_BARS];
+                if (!(i & 1)) mbar_expect_tx(full, 2 * C::TILE_BYTES);
                 const CUtensorMap* tm = (i & 1) ? &tmV : &tmK;
                 for (int x = 0; x < C::BOXES; x++)
-                    tma_load_4d(dst + x * BOX_BYTES, tm, &kvfull[slot], x * 64, (i >> 1) * BKEY,
-                                hk, b);
+                    tma_load_4d(dst + x * BOX_BYTES, tm, full, x * 64, (i >> 1) * BKEY, hk, b);
             }
             // drain: the releases of the last NSLOT items are tcgen05.commit
             // arrivals on this CTA's barriers; none may still be in flight
@@ -227,31 +232,39 @@ fmha_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
             const uint32_t sq_base = smem_u32(smem + C::Q_OFF);
             const uint32_t scol[2] = {C::S_COL0, C::S_COL1};
             const uint32_t ocol[2] = {C::O_COL0, C::O_COL1};
-            // ring slot and wait parity of K_j (item 2j) and V_j (item 2j+1)
+            // ring slot of K_j (item 2j) and V_j (item 2j+1); barrier and
+            // wait parity of step j's pair
             auto slot_of = [](int item) { return item % NSLOT; };
-            auto par_of = [](int item) { return (uint32_t)((item / NSLOT) & 1); };
+            auto kv_wait = [&](int j) {
+                return mbar_wait(&kvfull[j % KV_BARS], (uint32_t)((j / KV_BARS) & 1), abort_flag);
+            };
             auto slot_addr = [&](int item) {
                 return smem_u32(smem + C::KV_OFF + slot_of(item) * C::TILE_BYTES);
             };
+            // The issuing thread is held at each tcgen05.mma about as long as
+            // the MMA runs (N = 128), so the work between two MMAs is kept to
+            // constant adds: a descriptor's start-address field is addr >> 4
+            // in its low 14 bits, and a K step's byte offset adds to it
+            // without carrying out (shared addresses are below 256 KB).
             auto issue_qk = [&](int t, int j) {
-                const uint32_t kb = slot_addr(2 * j);
-                const uint32_t qb = sq_base + t * C::TILE_BYTES;
+                const uint64_t kd = sw128_desc(slot_addr(2 * j), 16, 1024);
+                const uint64_t qd = sw128_desc(sq_base + t * C::TILE_BYTES, 16, 1024);
+                const uint32_t s_tm = tmem_base + scol[t];
 #pragma unroll
                 for (int ks = 0; ks < D / 16; ks++) {
-                    const uint32_t off = (ks >> 2) * BOX_BYTES + (ks & 3) * 32;
-                    mma_f16_ss(tmem_base + scol[t], sw128_desc(qb + off, 16, 1024),
-                               sw128_desc(kb + off, 16, 1024), IDESC_QK, ks > 0 ? 1u : 0u);
+                    const uint64_t off = ((ks >> 2) * BOX_BYTES + (ks & 3) * 32) >> 4;
+                    mma_f16_ss(s_tm, qd + off, kd + off, IDESC_QK, ks > 0 ? 1u : 0u);
                 }
                 mma_commit(&sfull[t]);
             };
             // half 0: keys 0-63 of the tile, half 1: keys 64-127
             auto issue_pv = [&](int t, int j, int half) {
-                const uint32_t vb = slot_addr(2 * j + 1);
+                const uint64_t vd = sw128_desc(slot_addr(2 * j + 1), BOX_BYTES, 1024);
+                const uint32_t o_tm = tmem_base + ocol[t], p_tm = tmem_base + scol[t];
 #pragma unroll
                 for (int ks = half * (BKEY / 32); ks < (half + 1) * (BKEY / 32); ks++) {
                     // P: 16 keys = 8 packed TMEM columns per step; V: 16 key rows
-                    mma_f16_ts(tmem_base + ocol[t], tmem_base + scol[t] + ks * 8,
-                               sw128_desc(vb + ks * 16 * 128, BOX_BYTES, 1024), IDESC_PV,
+                    mma_f16_ts(o_tm, p_tm + ks * 8, vd + ((ks * 16 * 128) >> 4), IDESC_PV,
                                (j > 0 || ks > 0) ? 1u : 0u);
                 }
             };
@@ -261,7 +274,7 @@ fmha_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
             // come after every release, so a CTA whose softmax warps have
             // seen both ofinal has no commit arrival left in flight but the
             // ones the producer drains.
-            bool ok = mbar_wait(qfull, 0, abort_flag) && mbar_wait(&kvfull[0], 0, abort_flag);
+            bool ok = mbar_wait(qfull, 0, abort_flag) && kv_wait(0);
             if (ok) {
                 tc_fence_after();
                 if (nt0 > 0) issue_qk(0, 0);
@@ -269,26 +282,28 @@ fmha_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
                 mma_commit(&kvempty[slot_of(0)]);
             }
             for (int j = 0; ok && j < nmax; j++) {
-                if (!mbar_wait(&kvfull[slot_of(2 * j + 1)], par_of(2 * j + 1), abort_flag)) break;
                 bool have_next_k = false;
 #pragma unroll
                 for (int t = 0; t < 2; t++) {
                     const int ntt = t ? nt1 : nt0;
                     if (j >= ntt) continue;
                     const bool last_reader = t == 1 || j >= nt1;
-                    // P.V on the first half of P while the softmax finishes the second
-                    if (!mbar_wait(&phalf[t], j & 1, abort_flag)) { ok = false; break; }
+                    // P.V on the first half of P while the softmax finishes the
+                    // second (or on all of P at once: one wait fewer)
+                    if (p.half_p) {
+                        if (!flag_wait(&phalf[t], 4u * (j + 1), abort_flag)) { ok = false; break; }
+                        tc_fence_after();
+                        issue_pv(t, j, 0);
+                    }
+                    if (!flag_wait(&pready[t], 4u * (j + 1), abort_flag)) { ok = false; break; }
                     tc_fence_after();
-                    issue_pv(t, j, 0);
-                    if (!mbar_wait(&pready[t], j & 1, abort_flag)) { ok = false; break; }
-                    tc_fence_after();
+                    if (!p.half_p) issue_pv(t, j, 0);
                     issue_pv(t, j, 1);
                     if (last_reader) mma_commit(&kvempty[slot_of(2 * j + 1)]);
                     if (j + 1 == ntt) mma_commit(&ofinal[t]);
                     if (j + 1 < ntt) {
                         if (!have_next_k) {
-                            if (!mbar_wait(&kvfull[slot_of(2 * j + 2)], par_of(2 * j + 2),
-                                           abort_flag)) {
+                            if (!kv_wait(j + 1)) {
                                 ok = false;
                                 break;
                             }
@@ -393,7 +408,7 @@ fmha_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
                 tmem_wait_st();
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(half ? &pready[t] : &phalf[t]);
+                if (lane == 0) flag_add_release(half ? &pready[t] : &phalf[t]);
             }
             l += ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) +
                  ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
@@ -561,6 +576,7 @@ int fmha_fwd(const AttnDesc& d, cudaStream_t s) {
     p.scale_log2 = d.scale * 1.4426950408889634f;
     p.causal = d.causal ? 1 : 0;
     p.diag = d.diag;
+    p.half_p = getenv("ZBLAS_FMHA_NOHALF") ? 0 : 1;
     const long long grid = (long long)p.npairs * p.bh_count;
     if (grid > 0x7fffffffLL) return 1;
     if (d.d == 128)

@@ -644,10 +644,23 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                     const int buf = chunk & 1;
                     uint8_t* sbuf = epi + buf * C_::EPI_BUF;
                     if (leader) {
-                        bulk_wait_read<1>();           // store of chunk-2 has read sbuf
                         if (use_beta) {
-                            mbar_expect_tx(&cbar[buf], C_::EPI_BUF);
-                            tma_load_3d(sbuf, &tmC, &cbar[buf], m0, n0 + c0, b);
+                            // C chunks are loaded one chunk ahead: a tile's first
+                            // chunk here, chunk c+1 into the other buffer once the
+                            // store that last used it has read it
+                            if (c0 == 0) {
+                                bulk_wait_read<1>();   // store of chunk-2 has read sbuf
+                                mbar_expect_tx(&cbar[buf], C_::EPI_BUF);
+                                tma_load_3d(sbuf, &tmC, &cbar[buf], m0, n0 + c0, b);
+                            }
+                            if (c0 + kEpiCols < ncols) {
+                                bulk_wait_read<0>();   // store of chunk-1 has read the other buffer
+                                mbar_expect_tx(&cbar[buf ^ 1], C_::EPI_BUF);
+                                tma_load_3d(epi + (buf ^ 1) * C_::EPI_BUF, &tmC, &cbar[buf ^ 1], m0,
+                                            n0 + c0 + kEpiCols, b);
+                            }
+                        } else {
+                            bulk_wait_read<1>();       // store of chunk-2 has read sbuf
                         }
                     }
                     uint32_t v[32];

@@ -101,6 +101,41 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
     }
 }
 
+// Count-based hand-off between threads of one CTA through a 32-bit word in
+// shared memory: producers add 1 with release semantics, a consumer waits
+// until the word reaches `target` with acquire loads.  Cheaper for the
+// waiting thread than an mbarrier wait (a load, not a barrier operation);
+// not for TMA completions, which only an mbarrier can count.  Bounded like
+// mbar_wait.
+__device__ __forceinline__ void flag_add_release(uint32_t* flag) {
+    asm volatile("red.release.cta.shared::cta.add.u32 [%0], 1;" :: "r"(smem_u32(flag)) : "memory");
+}
+
+__device__ __forceinline__ uint32_t flag_load_acquire(uint32_t addr) {
+    uint32_t v;
+    asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ bool flag_wait(uint32_t* flag, uint32_t target, volatile int* abort) {
+    const uint32_t a = smem_u32(flag);
+    if (flag_load_acquire(a) >= target) return true;
+    const unsigned long long t0 = globaltimer();
+    uint32_t spins = 0;
+    while (true) {
+        __nanosleep(20);
+        if (flag_load_acquire(a) >= target) return true;
+        if ((++spins & 63u) == 0) {
+            if (*abort) return false;
+            if (globaltimer() - t0 > kWaitLimitNs) {
+                atomicCAS(&g_dev_error, 0, (int)kErrWaitTimeout);
+                *abort = 1;
+                return false;
+            }
+        }
+    }
+}
+
 // ---- TMA ------------------------------------------------------------------
 
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* m) {
