@@ -576,7 +576,9 @@ int fmha_fwd(const AttnDesc& d, cudaStream_t s) {
     p.scale_log2 = d.scale * 1.4426950408889634f;
     p.causal = d.causal ? 1 : 0;
     p.diag = d.diag;
-    p.half_p = getenv("ZBLAS_FMHA_NOHALF") ? 0 : 1;
+    // P.V on all of P at once (one wait per tile and key tile) measured 2-6 %
+    // faster than starting on its first half; ZBLAS_FMHA_HALF=1 restores that
+    p.half_p = getenv("ZBLAS_FMHA_HALF") ? 1 : 0;
     const long long grid = (long long)p.npairs * p.bh_count;
     if (grid > 0x7fffffffLL) return 1;
     if (d.d == 128)

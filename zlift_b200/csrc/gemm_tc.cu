@@ -126,32 +126,33 @@ __device__ __forceinline__ bool last_part(const TcParams& p, int slot) {
 // thread's row and 32 columns: part `own` is v (this CTA's accumulator);
 // the others come from `staged`, their 32 x 128 chunks one after another
 // in part order with `own` left out.  Part order makes the bits independent
-// of which part completed the tile.  Fully unrolled over 4 parts with
-// predicates, so v stays in registers.
+// of which part completed the tile.  16 columns at a time, parts in a loop,
+// a part's 16 loads unrolled so they are in flight together.
 template <int OUT>
 __device__ __forceinline__ void combine_parts(uint32_t (&v)[32], const uint32_t* staged,
                                               int split, int own, int row) {
-    const uint32_t* src_q[4];
 #pragma unroll
-    for (int q = 0; q < 4; q++)
-        src_q[q] = staged + (size_t)(q < own ? q : q - 1) * 32 * BM + row;
+    for (int h = 0; h < 2; h++) {
+        uint32_t acc[16];
+        const uint32_t* src = staged + row + h * 16 * BM;
+        for (int q = 0; q < split; q++) {
+            uint32_t x[16];
+            if (q == own) {
 #pragma unroll
-    for (int j = 0; j < 32; j++) {
-        uint32_t t[4];
+                for (int j = 0; j < 16; j++) x[j] = v[h * 16 + j];
+            } else {
 #pragma unroll
-        for (int q = 0; q < 4; q++)
-            t[q] = q == own ? v[j] : (q < split ? src_q[q][j * BM] : 0u);
-        if constexpr (OUT == kR32I) {
-            uint32_t a = t[0] + t[1];
-            if (split > 2) a += t[2];
-            if (split > 3) a += t[3];
-            v[j] = a;
-        } else {
-            float a = __uint_as_float(t[0]) + __uint_as_float(t[1]);
-            if (split > 2) a += __uint_as_float(t[2]);
-            if (split > 3) a += __uint_as_float(t[3]);
-            v[j] = __float_as_uint(a);
+                for (int j = 0; j < 16; j++) x[j] = src[j * BM];
+                src += 32 * BM;
+            }
+#pragma unroll
+            for (int j = 0; j < 16; j++) {
+                if constexpr (OUT == kR32I) acc[j] = q ? acc[j] + x[j] : x[j];
+                else acc[j] = q ? __float_as_uint(__uint_as_float(acc[j]) + __uint_as_float(x[j])) : x[j];
+            }
         }
+#pragma unroll
+        for (int j = 0; j < 16; j++) v[h * 16 + j] = acc[j];
     }
 }
 
