@@ -106,15 +106,16 @@ __device__ __forceinline__ Unit unit_of(const TcParams& p, int u) {
 // so a count left by an aborted launch reads as zero; the last part resets
 // it, so a CUDA graph replaying this launch with the same epoch starts from
 // zero too.  No CTA ever waits for another.
-__device__ __forceinline__ bool last_part(const TcParams& p, int slot) {
-    unsigned long long* c = p.counters + slot;
+__device__ __forceinline__ bool last_part(unsigned long long* counters, unsigned long long epoch,
+                                          int split, int slot) {
+    unsigned long long* c = counters + slot;
     unsigned long long cur = atomicAdd(c, 0ull);
     while (true) {
-        const unsigned long long done = (cur >> 16) == p.epoch ? (cur & 0xffffull) : 0ull;
-        const unsigned long long next = (p.epoch << 16) | (done + 1);
+        const unsigned long long done = (cur >> 16) == epoch ? (cur & 0xffffull) : 0ull;
+        const unsigned long long next = (epoch << 16) | (done + 1);
         const unsigned long long prev = atomicCAS(c, cur, next);
         if (prev == cur) {
-            if (done + 1 < (unsigned long long)p.split) return false;
+            if (done + 1 < (unsigned long long)split) return false;
             atomicExch(c, 0ull);
             return true;
         }
@@ -223,7 +224,8 @@ struct Cfg {
     static constexpr int PLANES = KT<KIND>::planes;
     static constexpr int STAGE_BYTES = (A_BYTES + B_BYTES) * PLANES;
     static constexpr int EPI_BUF = kEpiCols * BM * EPI_ES;     // one staging buffer
-    static constexpr int EPI_BYTES = 2 * EPI_BUF;
+    static constexpr int NEPI = 2;                              // staging buffers
+    static constexpr int EPI_BYTES = NEPI * EPI_BUF;
     static constexpr int STAGES_FIT = (kSmemBudget - kSmemReserve - EPI_BYTES) / STAGE_BYTES;
     static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
     static constexpr int TMEM_COLS = (2 * BN) < 32 ? 32 : (2 * BN);
@@ -339,6 +341,167 @@ __device__ __forceinline__ void store_out(void* C, long long at, uint32_t raw, u
             static_cast<__nv_bfloat16*>(C)[at] = __float2bfloat16_rn(v);
         }
     }
+}
+
+// alpha * acc (+ beta * C already in the staging buffer) (+ bias, act),
+// converted in place: this thread's row of one 32-column staging chunk
+// ([column][row], 128 rows).
+template <int OUT>
+__device__ __forceinline__ void convert_chunk(const uint32_t (&v)[32], uint8_t* sbuf, int row,
+                                              float alpha, float beta, int32_t ia, int32_t ib,
+                                              bool use_beta, int epi, float bias_row) {
+    constexpr int ES = out_es(OUT);
+#pragma unroll
+    for (int j = 0; j < 32; j++) {
+        uint8_t* e = sbuf + (j * BM + row) * ES;
+        if constexpr (OUT == kR32I) {
+            uint32_t x = (uint32_t)ia * v[j];
+            if (use_beta) x += (uint32_t)ib * *reinterpret_cast<uint32_t*>(e);
+            *reinterpret_cast<uint32_t*>(e) = x;
+        } else if constexpr (OUT == kR32F) {
+            float x = alpha * __uint_as_float(v[j]);
+            if (use_beta) x = fmaf(beta, *reinterpret_cast<float*>(e), x);
+            if (epi) x = apply_act(x + bias_row, epi);
+            *reinterpret_cast<float*>(e) = x;
+        } else if constexpr (OUT == kR16F) {
+            float x = alpha * __uint_as_float(v[j]);
+            if (use_beta) x = fmaf(beta, __half2float(*reinterpret_cast<__half*>(e)), x);
+            if (epi) x = apply_act(x + bias_row, epi);
+            *reinterpret_cast<__half*>(e) = __float2half_rn(x);
+        } else {
+            float x = alpha * __uint_as_float(v[j]);
+            if (use_beta)
+                x = fmaf(beta, __bfloat162float(*reinterpret_cast<__nv_bfloat16*>(e)), x);
+            if (epi) x = apply_act(x + bias_row, epi);
+            *reinterpret_cast<__nv_bfloat16*>(e) = __float2bfloat16_rn(x);
+        }
+    }
+}
+
+// What a K-split unit's epilogue needs (by value: the function below is
+// out of line, and taking the address of the kernel's parameters would make
+// the kernel copy them).
+struct SplitArgs {
+    uint32_t* work;
+    unsigned long long* counters;
+    unsigned long long epoch;
+    int split, tt, part, rank, ncols;
+    uint32_t taddr;
+    int m0, n0, b;
+    float alpha, beta, bias_row;
+    int32_t ia, ib;
+    int epi;
+    bool use_beta;
+};
+struct EpiState {
+    int chunk;
+    uint32_t cphase, rphase;
+    bool ok;
+};
+
+// Epilogue of a K-split unit, out of line so that the tile epilogue's hot
+// loop is compiled as if splits did not exist (inlined, its code cost the
+// 256 x 512^3 batched bf16 GEMM 35 %).  The part stores its partial sums
+// ([column][row] of this CTA's 128 rows), counts itself, and goes on only
+// if it completed the tile: then it copies the other parts' sums chunk by
+// chunk (32 columns, 16 KB per part) into the operand ring, idle by now (a
+// split unit is its CTA's last), up to three chunks ahead, adds them in part
+// order and runs the staged epilogue on the result.  Every sync point is
+// uniform over the 128 epilogue threads, as in the kernel.
+template <int BN, int OUT, bool PAIR, int NEPI, int EPI_BUF, int RING_BYTES>
+__device__ __noinline__ EpiState split_unit_epilogue(const SplitArgs a, EpiState st, uint8_t* smem,
+                                                     uint8_t* epi, uint64_t* cbar, uint64_t* rbar,
+                                                     volatile int* abort_flag,
+                                                     volatile int* split_last,
+                                                     const CUtensorMap* tmC, int row, int lane,
+                                                     bool leader) {
+    constexpr int RANKS = PAIR ? 2 : 1;
+    constexpr uint32_t kChunkBytes = 32 * BM * 4;
+    const size_t tile_words = (size_t)BN * BM;
+    uint32_t* mine = a.work + (((size_t)a.tt * a.split + a.part) * RANKS + a.rank) * tile_words;
+#pragma unroll 1
+    for (int c0 = 0; c0 < a.ncols; c0 += 32) {
+        uint32_t v[32];
+        tmem_ld32(a.taddr + c0, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 32; j++) __stcg(mine + (size_t)(c0 + j) * BM + row, v[j]);
+    }
+    __threadfence();
+    named_bar_sync(1, 128);
+    if (leader)
+        *split_last = last_part(a.counters, a.epoch, a.split, a.tt * RANKS + a.rank) ? 1 : 0;
+    named_bar_sync(1, 128);
+    if (!*split_last) return st;
+    __threadfence();
+    const int own = a.part;
+    const uint32_t* part0 = a.work + ((size_t)a.tt * a.split * RANKS + a.rank) * tile_words;
+    const int rslots = max(1, min(3, RING_BYTES / ((a.split - 1) * (int)kChunkBytes)));
+    auto fetch = [&](int c) {                  // leader: chunk c of the other parts
+        const int sl = c % rslots;
+        uint8_t* dst = smem + (size_t)sl * (a.split - 1) * kChunkBytes;
+        mbar_expect_tx(&rbar[sl], (uint32_t)(a.split - 1) * kChunkBytes);
+        for (int q = 0, i = 0; q < a.split; q++) {
+            if (q == own) continue;
+            bulk_load(dst + (size_t)i * kChunkBytes,
+                      part0 + (size_t)q * RANKS * tile_words + (size_t)c * 32 * BM, kChunkBytes,
+                      &rbar[sl]);
+            i++;
+        }
+    };
+    if (leader)
+        for (int c = 0; c < rslots && c * 32 < a.ncols; c++) fetch(c);
+#pragma unroll 1
+    for (int c0 = 0; c0 < a.ncols; c0 += kEpiCols, st.chunk++) {
+        const int buf = st.chunk % NEPI, nbuf = (st.chunk + 1) % NEPI;
+        uint8_t* sbuf = epi + buf * EPI_BUF;
+        if (leader) {
+            if (a.use_beta) {
+                if (c0 == 0) {
+                    bulk_wait_read<NEPI - 1>();
+                    mbar_expect_tx(&cbar[buf], EPI_BUF);
+                    tma_load_3d(sbuf, tmC, &cbar[buf], a.m0, a.n0 + c0, a.b);
+                }
+                if (c0 + kEpiCols < a.ncols) {
+                    bulk_wait_read<NEPI - 2>();
+                    mbar_expect_tx(&cbar[nbuf], EPI_BUF);
+                    tma_load_3d(epi + nbuf * EPI_BUF, tmC, &cbar[nbuf], a.m0,
+                                a.n0 + c0 + kEpiCols, a.b);
+                }
+            } else {
+                bulk_wait_read<NEPI - 1>();
+            }
+        }
+        uint32_t v[32];
+        tmem_ld32(a.taddr + c0, v);
+        bool w = true;
+        if (a.use_beta) {
+            w = mbar_wait(&cbar[buf], (st.cphase >> buf) & 1u, abort_flag);
+            st.cphase ^= 1u << buf;
+        }
+        const int sl = (c0 / 32) % rslots;
+        w = mbar_wait(&rbar[sl], (st.rphase >> sl) & 1u, abort_flag) && w;
+        st.rphase ^= 1u << sl;
+        tmem_wait_ld();
+        st.ok = named_bar_and(1, 128, w);
+        if (!st.ok) return st;
+        combine_parts<OUT>(v,
+                           reinterpret_cast<const uint32_t*>(smem + (size_t)sl * (a.split - 1) *
+                                                                        kChunkBytes),
+                           a.split, own, row);
+        convert_chunk<OUT>(v, sbuf, row, a.alpha, a.beta, a.ia, a.ib, a.use_beta, a.epi,
+                           a.bias_row);
+        fence_async_smem();
+        named_bar_sync(1, 128);
+        if (leader) {
+            tma_store_3d(tmC, sbuf, a.m0, a.n0 + c0, a.b);
+            bulk_commit();
+            // every thread has read ring slot sl: refill it
+            if (c0 + 32 * rslots < a.ncols) fetch(c0 / 32 + rslots);
+        }
+    }
+    (void)lane;
+    return st;
 }
 
 template <int KIND, int BN, bool A_MN, bool B_MN, int OUT, bool EPI_TMA, bool PAIR>
@@ -586,59 +749,41 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                 const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
                 const int ncols = min(BN, p.n - n0);
                 const float bias_row = load_bias(p, (long long)m0 + r_in_tile);
-                // K-split unit: store this part's partial sums ([column][row]
-                // of this CTA's 128 rows), count the part, and go on only if
-                // it completed the tile.  That part adds the other parts'
-                // sums, which it copies chunk by chunk (32 columns, 16 KB per
-                // part) into the operand ring, idle by now: a split unit is
-                // its CTA's last.  Up to `rslots` chunks are in flight.
-                constexpr int RANKS = PAIR ? 2 : 1;
-                constexpr uint32_t kChunkBytes = 32 * BM * 4;
-                const size_t tile_words = (size_t)BN * BM;
-                int own = -1;                          // >= 0: completing part
-                const uint32_t* part0 = nullptr;       // part 0's sums, this CTA's rows
-                int rslots = 0;
-                auto fetch = [&](int c) {              // leader: chunk c of the other parts
-                    const int sl = c % rslots;
-                    uint8_t* dst = smem + (size_t)sl * (p.split - 1) * kChunkBytes;
-                    mbar_expect_tx(&rbar[sl], (uint32_t)(p.split - 1) * kChunkBytes);
-                    for (int q = 0, i = 0; q < p.split; q++) {
-                        if (q == own) continue;
-                        bulk_load(dst + (size_t)i * kChunkBytes,
-                                  part0 + (size_t)q * RANKS * tile_words + (size_t)c * 32 * BM,
-                                  kChunkBytes, &rbar[sl]);
-                        i++;
-                    }
-                };
-                if (un.part >= 0) {
-                    const int tt = un.t - p.main_units;
-                    uint32_t* mine =
-                        p.work + (((size_t)tt * p.split + un.part) * RANKS + rank) * tile_words;
-#pragma unroll 1
-                    for (int c0 = 0; c0 < ncols; c0 += 32) {
-                        uint32_t v[32];
-                        tmem_ld32(taddr + c0, v);
-                        tmem_wait_ld();
-#pragma unroll
-                        for (int j = 0; j < 32; j++)
-                            __stcg(mine + (size_t)(c0 + j) * BM + r_in_tile, v[j]);
-                    }
-                    __threadfence();
-                    named_bar_sync(1, 128);
-                    if (leader) *split_last = last_part(p, tt * RANKS + (int)rank) ? 1 : 0;
-                    named_bar_sync(1, 128);
-                    if (!*split_last) {
-                        tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0) release_acc(&tempty[acc], rank);
-                        continue;
-                    }
-                    __threadfence();
-                    own = un.part;
-                    part0 = p.work + ((size_t)tt * p.split * RANKS + rank) * tile_words;
-                    rslots = max(1, min(3, (STAGES * STAGE_BYTES) / ((p.split - 1) * (int)kChunkBytes)));
-                    if (leader)
-                        for (int c = 0; c < rslots && c * 32 < ncols; c++) fetch(c);
+                if (un.part >= 0) {             // K-split unit: out of line
+                    SplitArgs sa;
+                    sa.work = p.work;
+                    sa.counters = p.counters;
+                    sa.epoch = p.epoch;
+                    sa.split = p.split;
+                    sa.tt = un.t - p.main_units;
+                    sa.part = un.part;
+                    sa.rank = (int)rank;
+                    sa.ncols = ncols;
+                    sa.taddr = taddr;
+                    sa.m0 = m0;
+                    sa.n0 = n0;
+                    sa.b = b;
+                    sa.alpha = alpha;
+                    sa.beta = beta;
+                    sa.bias_row = bias_row;
+                    sa.ia = ia;
+                    sa.ib = ib;
+                    sa.epi = p.epi;
+                    sa.use_beta = use_beta;
+                    EpiState es{chunk, cphase, rphase, true};
+                    es = split_unit_epilogue<BN, OUT, PAIR, C_::NEPI, C_::EPI_BUF,
+                                             STAGES * STAGE_BYTES>(
+                        sa, es, smem, epi, cbar, rbar, abort_flag, split_last, &tmC, r_in_tile,
+                        lane, leader);
+                    chunk = es.chunk;
+                    cphase = es.cphase;
+                    rphase = es.rphase;
+                    ok = es.ok;
+                    if (!ok) break;
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) release_acc(&tempty[acc], rank);
+                    continue;
                 }
 #pragma unroll 1
                 for (int c0 = 0; c0 < ncols; c0 += kEpiCols, chunk++) {
@@ -671,51 +816,16 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                         w = mbar_wait(&cbar[buf], (cphase >> buf) & 1u, abort_flag);
                         cphase ^= 1u << buf;
                     }
-                    const int sl = own >= 0 ? (c0 / 32) % rslots : 0;
-                    if (own >= 0) {
-                        w = mbar_wait(&rbar[sl], (rphase >> sl) & 1u, abort_flag) && w;
-                        rphase ^= 1u << sl;
-                    }
                     tmem_wait_ld();
                     ok = named_bar_and(1, 128, w);
                     if (!ok) break;
-                    if (own >= 0)
-                        combine_parts<OUT>(v,
-                                           reinterpret_cast<const uint32_t*>(
-                                               smem + (size_t)sl * (p.split - 1) * kChunkBytes),
-                                           p.split, own, r_in_tile);
-#pragma unroll
-                    for (int j = 0; j < 32; j++) {
-                        uint8_t* e = sbuf + (j * BM + r_in_tile) * ES;
-                        if constexpr (OUT == kR32I) {
-                            uint32_t x = (uint32_t)ia * v[j];
-                            if (use_beta) x += (uint32_t)ib * *reinterpret_cast<uint32_t*>(e);
-                            *reinterpret_cast<uint32_t*>(e) = x;
-                        } else if constexpr (OUT == kR32F) {
-                            float x = alpha * __uint_as_float(v[j]);
-                            if (use_beta) x = fmaf(beta, *reinterpret_cast<float*>(e), x);
-                            if (p.epi) x = apply_act(x + bias_row, p.epi);
-                            *reinterpret_cast<float*>(e) = x;
-                        } else if constexpr (OUT == kR16F) {
-                            float x = alpha * __uint_as_float(v[j]);
-                            if (use_beta) x = fmaf(beta, __half2float(*reinterpret_cast<__half*>(e)), x);
-                            if (p.epi) x = apply_act(x + bias_row, p.epi);
-                            *reinterpret_cast<__half*>(e) = __float2half_rn(x);
-                        } else {
-                            float x = alpha * __uint_as_float(v[j]);
-                            if (use_beta)
-                                x = fmaf(beta, __bfloat162float(*reinterpret_cast<__nv_bfloat16*>(e)), x);
-                            if (p.epi) x = apply_act(x + bias_row, p.epi);
-                            *reinterpret_cast<__nv_bfloat16*>(e) = __float2bfloat16_rn(x);
-                        }
-                    }
+                    convert_chunk<OUT>(v, sbuf, r_in_tile, alpha, beta, ia, ib, use_beta, p.epi,
+                                       bias_row);
                     fence_async_smem();
                     named_bar_sync(1, 128);
                     if (leader) {
                         tma_store_3d(&tmC, sbuf, m0, n0 + c0, b);
                         bulk_commit();
-                        // every thread has read ring slot sl: refill it
-                        if (own >= 0 && c0 + 32 * rslots < ncols) fetch(c0 / 32 + rslots);
                     }
                 }
                 tc_fence_before();
@@ -911,7 +1021,8 @@ constexpr bool pair_ok(int kind, int bn) {
 
 // K split of the last wave.  `tiles` tiles on `slots` persistent CTAs (or
 // pairs) leave the last wave R = tiles % slots tiles; when R is at most half
-// of the slots, each of those tiles is split into S = min(slots / R, 4)
+// of the slots (and, by default, there is no full wave before it), each of
+// those tiles is split into S = min(slots / R, 4)
 // parts along K (each part at least 4 K blocks), so the last wave takes
 // about 1/S of a tile's time.  `unit_bytes` is the workspace one part of
 // one tile needs (0: this configuration does not split).  The part that
@@ -921,16 +1032,24 @@ constexpr bool pair_ok(int kind, int bn) {
 void split_tail(TcParams& q, int tiles, int slots, size_t unit_bytes, size_t ring_bytes) {
     q.main_units = q.total_units = tiles;
     q.split = 1;
-    const char* on = getenv("ZBLAS_SPLIT_K");           // opt-in for now
-    if (!on || on[0] == '0') return;
+    // ZBLAS_SPLIT_K: unset = split only a GEMM that is one sparse wave (fewer
+    // tiles than half the CTAs: small m x n, long k); 1 = also the sparse
+    // last wave after full waves (measured slower on 4096^3); 0 = never
+    const char* sw = getenv("ZBLAS_SPLIT_K");
+    if (sw && sw[0] == '0') return;
+    const bool tails = sw && sw[0] == '1';
     if (!q.work || !q.counters || unit_bytes == 0 || slots <= 1) return;
     const int rem = tiles % slots;
     if (rem == 0 || 2 * rem > slots) return;
+    if (tiles >= slots && !tails) return;
     int parts = slots / rem;
     if (parts > 4) parts = 4;
     while (parts > 1 && (q.k_blocks / parts < 4 || (size_t)(parts - 1) * 32 * BM * 4 > ring_bytes))
         parts--;
     if (parts < 2 || (size_t)rem * parts * unit_bytes > q.work_bytes) return;
+    // two parts halve the main loop but not the completing part's epilogue,
+    // which then also sums them: 1024 x 1024 x 4096 was slower split in two
+    if (parts < 3 && !tails) return;
     q.split = parts;
     q.main_units = tiles - rem;
     q.total_units = q.main_units + rem * parts;
