@@ -168,6 +168,21 @@ ZLIFT_API int zlift_device_error(void);
 /* Number of kernels this library launched on any stream since load. */
 ZLIFT_API unsigned long long zlift_launch_count(void);
 
+/* Time limit, in nanoseconds, of every bounded device-side wait of this
+ * library's kernels on the current device (default 2 s).  A wait that runs
+ * out records error 1 (see zlift_device_error), makes its kernel leave its
+ * loops and return; the context stays usable.  ns = 0 is INVALID_VALUE. */
+ZLIFT_API int zlift_set_wait_limit_ns(unsigned long long ns);
+ZLIFT_API unsigned long long zlift_get_wait_limit_ns(void);
+
+/* Failure-path check: launches on `stream` a one-thread kernel whose
+ * mbarrier wait nothing completes, bounded by limit_ns (at most 10 s).  It
+ * returns after the limit with error 1 recorded for zlift_device_error.
+ * The reference's failure handling is decline-then-fallback
+ * (zblas/zblas_gpu.cpp:184-201); this exercises the build's replacement,
+ * the bounded wait, without faulting or hanging the GPU. */
+ZLIFT_API int zlift_wait_probe(unsigned long long limit_ns, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -28,9 +28,10 @@ _vp, _int, _ll, _f, _d = (ctypes.c_void_p, ctypes.c_int, ctypes.c_longlong, ctyp
                           ctypes.c_double)
 
 
-def build(ref: bool = False) -> None:
-    """Runs the Makefile (`make`, or `make ref` when the reference tree is
-    present and `ref` is asked for)."""
+def build(ref: bool = True) -> None:
+    """Runs the Makefile: `make ref` builds the restatement and, where the
+    reference sources are found (the recipe's REF), the reference's own CPU
+    path; `make` only the restatement."""
     target = ["ref"] if ref else []
     subprocess.run(["make", "-s", "-C", HERE] + target, check=True,
                    stdout=subprocess.DEVNULL)

@@ -136,11 +136,20 @@ static double load_elem(const void *p, int type, int64_t at) {
     }
 }
 
+static int gemm_wide(int transa, int transb, int m, int n, int k, float alpha,
+                     const void *A, int Atype, int lda, const void *B, int Btype,
+                     int ldb, float beta, void *C, int Ctype, int ldc);
+
 /* fp32 GEMM restating cblas_sgemm (zblas/zblas.c:127): C = alpha*op(A)op(B)
- * + beta*C, column-major.  beta == 0 does not read C (BLAS convention). */
+ * + beta*C, column-major.  beta == 0 does not read C (BLAS convention).
+ * Products are summed in fp64 and rounded once (gemm_wide); the plain loop
+ * below only runs if the packed copies cannot be allocated. */
 void zo_sgemm(int transa, int transb, int m, int n, int k, float alpha,
               const float *A, int lda, const float *B, int ldb, float beta,
               float *C, int ldc) {
+    if (gemm_wide(transa, transb, m, n, k, alpha, A, ZO_R_32F, lda, B, ZO_R_32F, ldb,
+                  beta, C, ZO_R_32F, ldc) == ZO_OK)
+        return;
 #pragma omp parallel for schedule(static)
     for (int j = 0; j < n; j++) {
         for (int i = 0; i < m; i++) {
@@ -155,47 +164,122 @@ void zo_sgemm(int transa, int transb, int m, int n, int k, float alpha,
     }
 }
 
-/* int8 x int8 -> int32 with int32 alpha/beta; exact, wrapping. */
+/* Dot product of two int8 vectors with int32 wrap-around accumulation.
+ * Accumulating in 32 bits modulo 2^32 gives the same low 32 bits as an
+ * exact (wider) sum, which is all the int32 result keeps.  Written so the
+ * compiler vectorises it; the clones pick AVX2 / AVX-512 where the host
+ * has them. */
+__attribute__((target_clones("arch=skylake-avx512", "avx2", "default")))
+static uint32_t dot_i8(const int8_t *a, const int8_t *b, int k) {
+    uint32_t acc = 0;
+    for (int l = 0; l < k; l++)
+        acc += (uint32_t)((int32_t)a[l] * (int32_t)b[l]);
+    return acc;
+}
+
+/* op(X) as a dense [rows][k] int8 array (K contiguous). */
+static int8_t *pack_i8(int op, const int8_t *X, int rows, int k, int ld, int is_b) {
+    int8_t *p = malloc((size_t)rows * (size_t)(k > 0 ? k : 1));
+    if (!p) return NULL;
+#pragma omp parallel for schedule(static)
+    for (int r = 0; r < rows; r++)
+        for (int l = 0; l < k; l++)
+            /* A: op(A)(r, l); B: op(B)(l, r) */
+            p[(size_t)r * k + l] = is_b ? X[opidx(op, l, r, ld)] : X[opidx(op, r, l, ld)];
+    return p;
+}
+
+/* int8 x int8 -> int32 with int32 alpha/beta; exact, wrapping.  Both
+ * operands are packed K-contiguous, then 64 x 64 blocks of C are computed
+ * from cache-resident rows. */
 static void gemm_i8(int transa, int transb, int m, int n, int k,
                     int32_t alpha, const int8_t *A, int lda,
                     const int8_t *B, int ldb, int32_t beta,
                     int32_t *C, int ldc) {
-#pragma omp parallel for schedule(static)
-    for (int j = 0; j < n; j++) {
-        for (int i = 0; i < m; i++) {
-            int64_t acc = 0;
-            for (int l = 0; l < k; l++)
-                acc += (int32_t)A[opidx(transa, i, l, lda)]
-                     * (int32_t)B[opidx(transb, l, j, ldb)];
-            uint32_t r = (uint32_t)alpha * (uint32_t)(int32_t)acc;
-            if (beta != 0)
-                r += (uint32_t)beta * (uint32_t)C[i + (int64_t)j * ldc];
-            C[i + (int64_t)j * ldc] = (int32_t)r;
+    int8_t *pa = pack_i8(transa, A, m, k, lda, 0);
+    int8_t *pb = pack_i8(transb, B, n, k, ldb, 1);
+    if (!pa || !pb) { free(pa); free(pb); return; }
+    const int T = 64;
+    const int bm = (m + T - 1) / T, bn = (n + T - 1) / T;
+#pragma omp parallel for schedule(dynamic, 1)
+    for (int64_t blk = 0; blk < (int64_t)bm * bn; blk++) {
+        const int i0 = (int)(blk % bm) * T, j0 = (int)(blk / bm) * T;
+        const int i1 = i0 + T < m ? i0 + T : m, j1 = j0 + T < n ? j0 + T : n;
+        for (int j = j0; j < j1; j++) {
+            const int8_t *bj = pb + (size_t)j * k;
+            for (int i = i0; i < i1; i++) {
+                uint32_t r = (uint32_t)alpha * dot_i8(pa + (size_t)i * k, bj, k);
+                if (beta != 0)
+                    r += (uint32_t)beta * (uint32_t)C[i + (int64_t)j * ldc];
+                C[i + (int64_t)j * ldc] = (int32_t)r;
+            }
         }
     }
+    free(pa);
+    free(pb);
+}
+
+/* fp64 dot product with four partial sums (fixed order: the result does
+ * not depend on the host or the thread count). */
+__attribute__((target_clones("arch=skylake-avx512", "avx2", "default")))
+static double dot_f64(const double *a, const double *b, int k) {
+    double s0 = 0.0, s1 = 0.0, s2 = 0.0, s3 = 0.0;
+    int l = 0;
+    for (; l + 4 <= k; l += 4) {
+        s0 += a[l] * b[l];
+        s1 += a[l + 1] * b[l + 1];
+        s2 += a[l + 2] * b[l + 2];
+        s3 += a[l + 3] * b[l + 3];
+    }
+    for (; l < k; l++) s0 += a[l] * b[l];
+    return (s0 + s1) + (s2 + s3);
+}
+
+/* op(X) widened to a dense [rows][k] fp64 array (K contiguous), through
+ * the reference converters. */
+static double *pack_wide(int op, const void *X, int type, int rows, int k, int ld, int is_b) {
+    double *p = malloc(sizeof(double) * (size_t)rows * (size_t)(k > 0 ? k : 1));
+    if (!p) return NULL;
+#pragma omp parallel for schedule(static)
+    for (int r = 0; r < rows; r++)
+        for (int l = 0; l < k; l++)
+            p[(size_t)r * k + l] = is_b ? load_elem(X, type, opidx(op, l, r, ld))
+                                        : load_elem(X, type, opidx(op, r, l, ld));
+    return p;
 }
 
 /* 16-bit (or fp32) inputs, fp32 compute: restates gemm_ex_host
- * (zblas/zblas.c:318-356) -- widen, fp32 GEMM, narrow C. */
+ * (zblas/zblas.c:318-356) -- widen, fp32 GEMM, narrow C.  The products are
+ * summed in fp64 and rounded once to fp32 (at least as accurate as the
+ * single-precision BLAS the reference calls), then narrowed with the
+ * reference converter. */
 static int gemm_wide(int transa, int transb, int m, int n, int k, float alpha,
                      const void *A, int Atype, int lda, const void *B, int Btype,
                      int ldb, float beta, void *C, int Ctype, int ldc) {
-#pragma omp parallel for schedule(static)
-    for (int j = 0; j < n; j++) {
-        for (int i = 0; i < m; i++) {
-            double acc = 0.0;
-            for (int l = 0; l < k; l++)
-                acc += load_elem(A, Atype, opidx(transa, i, l, lda))
-                     * load_elem(B, Btype, opidx(transb, l, j, ldb));
-            int64_t at = i + (int64_t)j * ldc;
-            double c = (double)alpha * acc;
-            if (beta != 0.0f) c += (double)beta * load_elem(C, Ctype, at);
-            float cf = (float)c;
-            if (Ctype == ZO_R_16F) ((uint16_t *)C)[at] = zo_float_to_half(cf);
-            else if (Ctype == ZO_R_16BF) ((uint16_t *)C)[at] = zo_float_to_bf16(cf);
-            else ((float *)C)[at] = cf;
+    double *pa = pack_wide(transa, A, Atype, m, k, lda, 0);
+    double *pb = pack_wide(transb, B, Btype, n, k, ldb, 1);
+    if (!pa || !pb) { free(pa); free(pb); return ZO_NOT_INITIALIZED; }
+    const int T = 32;
+    const int bm = (m + T - 1) / T, bn = (n + T - 1) / T;
+#pragma omp parallel for schedule(dynamic, 1)
+    for (int64_t blk = 0; blk < (int64_t)bm * bn; blk++) {
+        const int i0 = (int)(blk % bm) * T, j0 = (int)(blk / bm) * T;
+        const int i1 = i0 + T < m ? i0 + T : m, j1 = j0 + T < n ? j0 + T : n;
+        for (int j = j0; j < j1; j++) {
+            for (int i = i0; i < i1; i++) {
+                double acc = dot_f64(pa + (size_t)i * k, pb + (size_t)j * k, k);
+                int64_t at = i + (int64_t)j * ldc;
+                double c = (double)alpha * acc;
+                if (beta != 0.0f) c += (double)beta * load_elem(C, Ctype, at);
+                float cf = (float)c;
+                if (Ctype == ZO_R_16F) ((uint16_t *)C)[at] = zo_float_to_half(cf);
+                else if (Ctype == ZO_R_16BF) ((uint16_t *)C)[at] = zo_float_to_bf16(cf);
+                else ((float *)C)[at] = cf;
+            }
         }
     }
+    free(pa);
+    free(pb);
     return ZO_OK;
 }
 

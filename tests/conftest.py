@@ -35,7 +35,7 @@ def built_lib():
 def oracle_lib():
     from oracle import oracle
     if not os.path.exists(oracle.ORACLE_SO):
-        oracle.build(ref=os.path.isdir("/root/reference"))
+        oracle.build(ref=True)
     return oracle
 
 

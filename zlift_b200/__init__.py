@@ -60,6 +60,9 @@ SIGNATURES = [
                                     c_int]),
     ("zlift_device_error", c_int, []),
     ("zlift_launch_count", ctypes.c_ulonglong, []),
+    ("zlift_set_wait_limit_ns", c_int, [ctypes.c_ulonglong]),
+    ("zlift_get_wait_limit_ns", ctypes.c_ulonglong, []),
+    ("zlift_wait_probe", c_int, [ctypes.c_ulonglong, c_void_p]),
     ("zblas_gpu_flash_f16", c_int, [c_void_p, c_uint, c_int]),
     ("zblas_gpu_fmha_f16", c_int, [c_void_p, c_uint, c_int]),
     ("zblas_attention_set_stream", None, [c_void_p]),

@@ -58,8 +58,16 @@ struct Handle {
     size_t user_ws_bytes = 0;
     void* scratch = nullptr;         // library-owned, grown on demand
     size_t scratch_bytes = 0;
-    void* split_ws = nullptr;        // K-split tail workspace (counters, then partials)
-    unsigned long long split_epoch = 0;
+    // K-split tail workspaces (counters, then partial sums), one per stream
+    // the handle has launched split GEMMs on, so that split launches on
+    // different streams never share counters
+    struct SplitWs {
+        cudaStream_t stream = nullptr;
+        void* ws = nullptr;
+        unsigned long long epoch = 0;
+    };
+    static constexpr int kSplitStreams = 4;
+    SplitWs split[kSplitStreams];
     std::mutex mu;
 };
 
@@ -104,14 +112,23 @@ static cublasStatus_t map_launch(int rc) {
 
 // Workspace of the tensor-core kernel's K-split tail (GemmDesc::split_work):
 // tile counters, then partial sums; the largest split needs 2 * 74 parts of
-// 128 x 256 fp32 values (18.9 MB).  Allocated on the handle's first GEMM,
-// except inside a stream capture, where the GEMM goes without it.  Each
-// launch gets the next epoch.  Called with h->mu held.
+// 128 x 256 fp32 values (18.9 MB).  One workspace per stream (up to
+// kSplitStreams streams per handle; calls on further streams run without a
+// split), allocated on the first GEMM on that stream, except inside a
+// stream capture, where the GEMM goes without it.  Each launch gets the
+// next epoch of its stream's workspace.  Called with h->mu held.
 constexpr size_t kSplitCounterBytes = 4096;
 constexpr size_t kSplitWorkBytes = 20u << 20;
 
 static void attach_split_ws(Handle* h, GemmDesc& d, cudaStream_t s) {
-    if (!h->split_ws) {
+    Handle::SplitWs* w = nullptr;
+    for (auto& x : h->split)
+        if (x.ws && x.stream == s) w = &x;
+    if (!w) {
+        Handle::SplitWs* slot = nullptr;
+        for (auto& x : h->split)
+            if (!x.ws && !slot) slot = &x;
+        if (!slot) return;
         cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
         if (cudaStreamIsCapturing(s, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) {
             cudaGetLastError();
@@ -127,12 +144,15 @@ static void attach_split_ws(Handle* h, GemmDesc& d, cudaStream_t s) {
             cudaFree(p);
             return;
         }
-        h->split_ws = p;
+        slot->stream = s;
+        slot->ws = p;
+        slot->epoch = 0;
+        w = slot;
     }
-    d.split_counters = static_cast<unsigned long long*>(h->split_ws);
-    d.split_work = reinterpret_cast<uint32_t*>(static_cast<char*>(h->split_ws) + kSplitCounterBytes);
+    d.split_counters = static_cast<unsigned long long*>(w->ws);
+    d.split_work = reinterpret_cast<uint32_t*>(static_cast<char*>(w->ws) + kSplitCounterBytes);
     d.split_work_bytes = kSplitWorkBytes;
-    d.split_epoch = ++h->split_epoch;
+    d.split_epoch = ++w->epoch;
 }
 
 // Runs one validated GEMM description: tensor cores first, CUDA cores when
@@ -299,12 +319,15 @@ cublasStatus_t cublasCreate_v2(cublasHandle_t* handle) {
 cublasStatus_t cublasDestroy_v2(cublasHandle_t handle) {
     Handle* h = as_handle(handle);
     if (!h) return CUBLAS_STATUS_NOT_INITIALIZED;
-    if (h->scratch || h->split_ws) {
+    bool any = h->scratch != nullptr;
+    for (auto& x : h->split) any = any || x.ws;
+    if (any) {
         int cur = 0;
         cudaGetDevice(&cur);
         cudaSetDevice(h->device);
         if (h->scratch) cudaFree(h->scratch);
-        if (h->split_ws) cudaFree(h->split_ws);
+        for (auto& x : h->split)
+            if (x.ws) cudaFree(x.ws);
         cudaSetDevice(cur);
     }
     h->magic = 0;
@@ -740,5 +763,19 @@ int zlift_device_error(void) {
 }
 
 unsigned long long zlift_launch_count(void) { return launch_count(); }
+
+int zlift_set_wait_limit_ns(unsigned long long ns) {
+    if (ns == 0) return CUBLAS_STATUS_INVALID_VALUE;
+    const int r = gemm_tc_set_wait_limit(ns) | gemm_simt_set_wait_limit(ns) |
+                  fmha_set_wait_limit(ns);
+    return r ? CUBLAS_STATUS_EXECUTION_FAILED : CUBLAS_STATUS_SUCCESS;
+}
+
+unsigned long long zlift_get_wait_limit_ns(void) { return wait_limit_ns(); }
+
+int zlift_wait_probe(unsigned long long limit_ns, void* stream) {
+    if (limit_ns == 0 || limit_ns > 10000000000ull) return CUBLAS_STATUS_INVALID_VALUE;
+    return map_launch(wait_probe(limit_ns, static_cast<cudaStream_t>(stream)));
+}
 
 }  // extern "C"

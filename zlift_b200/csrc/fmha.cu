@@ -588,6 +588,8 @@ int fmha_fwd(const AttnDesc& d, cudaStream_t s) {
                        : launch<64, false>(d, tq, tk, tv, p, grid, s);
 }
 
+int fmha_set_wait_limit(unsigned long long ns) { return set_unit_wait_limit(ns); }
+
 int fmha_error(bool clear) {
     int v = 0;
     cudaMemcpyFromSymbol(&v, g_dev_error, sizeof(int));

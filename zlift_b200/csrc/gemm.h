@@ -99,6 +99,13 @@ unsigned long long launch_count();
 
 // Device error words of the kernel translation units (read, optionally clear).
 int gemm_tc_error(bool clear);
+int gemm_tc_set_wait_limit(unsigned long long ns);
+int gemm_simt_set_wait_limit(unsigned long long ns);
+int fmha_set_wait_limit(unsigned long long ns);
+unsigned long long wait_limit_ns();
+// Launches a one-thread kernel whose mbarrier wait nobody completes: it
+// gives up after limit_ns, records kErrWaitTimeout and returns.
+int wait_probe(unsigned long long limit_ns, cudaStream_t s);
 int gemm_simt_error(bool clear);
 int fmha_error(bool clear);
 

@@ -221,6 +221,32 @@ int split_tf32(const float* X, bool k_contig, long long MN, long long K, long lo
     return e == cudaSuccess ? 0 : (int)e;
 }
 
+// A wait that nothing completes: one thread initialises an mbarrier that
+// expects one arrival and waits on its first phase with `limit_ns`.  No
+// copy or MMA is in flight, so the kernel simply returns after the limit,
+// with kErrWaitTimeout in this unit's error word.
+__global__ void wait_probe_kernel(unsigned long long limit_ns) {
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ int abort_flag;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        abort_flag = 0;
+        fence_mbar_init();
+        mbar_wait_for(&bar, 0, &abort_flag, limit_ns);
+    }
+}
+
+int wait_probe(unsigned long long limit_ns, cudaStream_t s) {
+    wait_probe_kernel<<<1, 32, 0, s>>>(limit_ns);
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) note_launch();
+    return e == cudaSuccess ? 0 : (int)e;
+}
+
+unsigned long long wait_limit_ns() { return get_unit_wait_limit(); }
+
+int gemm_simt_set_wait_limit(unsigned long long ns) { return set_unit_wait_limit(ns); }
+
 int gemm_simt_error(bool clear) {
     int v = 0;
     cudaMemcpyFromSymbol(&v, g_dev_error, sizeof(int));

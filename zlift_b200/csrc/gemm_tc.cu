@@ -427,6 +427,8 @@ __device__ __noinline__ EpiState split_unit_epilogue(const SplitArgs a, EpiState
 #pragma unroll
         for (int j = 0; j < 32; j++) __stcg(mine + (size_t)(c0 + j) * BM + row, v[j]);
     }
+    // the partial sums are read by another CTA's bulk copies (async proxy)
+    fence_async_global();
     __threadfence();
     named_bar_sync(1, 128);
     if (leader)
@@ -434,6 +436,9 @@ __device__ __noinline__ EpiState split_unit_epilogue(const SplitArgs a, EpiState
     named_bar_sync(1, 128);
     if (!*split_last) return st;
     __threadfence();
+    // the other parts' plain stores, acquired through the counter, before
+    // this CTA's bulk copies read them
+    fence_async_global();
     const int own = a.part;
     const uint32_t* part0 = a.work + ((size_t)a.tt * a.split * RANKS + a.rank) * tile_words;
     const int rslots = max(1, min(3, RING_BYTES / ((a.split - 1) * (int)kChunkBytes)));
@@ -1303,6 +1308,8 @@ int gemm_tc(const GemmDesc& d, cudaStream_t s) {
     }
     return 1;
 }
+
+int gemm_tc_set_wait_limit(unsigned long long ns) { return set_unit_wait_limit(ns); }
 
 int gemm_tc_error(bool clear) {
     int v = 0;

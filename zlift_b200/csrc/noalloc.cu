@@ -20,8 +20,10 @@
 // 16 MiB exactly.)
 //
 // The first call on a device looks up that device's address of the array
-// (cudaGetSymbolAddress, with the device current) and caches it; make that
-// first call before any stream capture begins.  Every call on a device
+// (cudaGetSymbolAddress, with the device current) and caches it, tagged
+// with the current context (a new context -- after cudaDeviceReset, say --
+// looks it up again); make that first call before any stream capture
+// begins.  Every call on a device
 // shares the one array and overwrites all of the planes it reads, so no
 // call depends on what an earlier call left there -- but two calls whose
 // kernels overlap on the GPU (different streams, or different host
@@ -29,6 +31,8 @@
 #include "gemm.h"
 
 #include "../../include/zlift_cublas.h"
+
+#include <cuda.h>
 
 #include <cstdio>
 #include <mutex>
@@ -40,18 +44,59 @@ constexpr size_t kScratchBytes = size_t(16) << 20;
 static __device__ __align__(256) float g_noalloc_scratch[kScratchBytes / sizeof(float)];
 
 std::mutex g_mu;
-void* g_addr[64] = {nullptr};
 
-// Device address of g_noalloc_scratch on the current device (looked up
-// once per device).  Host code may not use the array's name as an address.
+// The driver's cuCtxGetCurrent, looked up once (the library links only the
+// runtime).
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+CtxGetCurrentFn ctx_get_current() {
+    static CtxGetCurrentFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) ==
+                cudaSuccess && q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<CtxGetCurrentFn>(f);
+        else
+            cudaGetLastError();
+    });
+    return fn;
+}
+
+// One cached address per device, tagged with the context it was looked up
+// in: after cudaDeviceReset, or under another context on the same device,
+// the array lives at a new address and is looked up again.
+struct Cached {
+    CUcontext ctx = nullptr;
+    void* addr = nullptr;
+};
+Cached g_addr[64];
+
+// Device address of g_noalloc_scratch in the current context.  Host code
+// may not use the array's name as an address.
 float* scratch_on_current_device() {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
         cudaGetLastError();
         return nullptr;
     }
+    CUcontext ctx = nullptr;
+    CtxGetCurrentFn get = ctx_get_current();
+    if (get && get(&ctx) == CUDA_SUCCESS && !ctx) {
+        // no context yet on this thread: the symbol lookup creates the
+        // device's primary context as a side effect
+        void* p = nullptr;
+        cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        cudaGetLastError();
+        get(&ctx);
+    }
+    if (!get || !ctx) {
+        fprintf(stderr, "[zblas] zlift_sgemm_noalloc: no current CUDA context\n");
+        return nullptr;
+    }
     std::lock_guard<std::mutex> lock(g_mu);
-    if (!g_addr[dev]) {
+    Cached& c = g_addr[dev];
+    if (!c.addr || c.ctx != ctx) {
         void* p = nullptr;
         cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
         if (e != cudaSuccess || !p) {
@@ -60,9 +105,10 @@ float* scratch_on_current_device() {
                     cudaGetErrorString(e));
             return nullptr;
         }
-        g_addr[dev] = p;
+        c.ctx = ctx;
+        c.addr = p;
     }
-    return static_cast<float*>(g_addr[dev]);
+    return static_cast<float*>(c.addr);
 }
 
 cublasStatus_t done(int rc) {
@@ -113,12 +159,26 @@ extern "C" cublasStatus_t zlift_sgemm_noalloc(cublasHandle_t handle, int transa,
     const bool two = d.kind == Kind::TF32X3;
     const long long kp = ((long long)k + 3) & ~3ll;
     auto up = [](long long e) { return (e + 63) & ~63ll; };
-    const long long ea = up((long long)m * kp), eb = up((long long)n * kp);
-    const unsigned long long need = (unsigned long long)((two ? 2 : 1) * (ea + eb)) * sizeof(float);
-    if (need > kScratchBytes) {
+    // Size check without overflow: every factor is bounded before the
+    // products are formed (m, n < 2^31 and kp < 2^31 + 4, so m*kp < 2^63;
+    // each plane is then compared with the array before they are summed).
+    const unsigned long long cap = kScratchBytes / sizeof(float);     // floats in the array
+    const unsigned long long ea_u = (unsigned long long)m * (unsigned long long)kp;
+    const unsigned long long eb_u = (unsigned long long)n * (unsigned long long)kp;
+    const unsigned long long planes = two ? 2 : 1;
+    bool fits = ea_u <= cap && eb_u <= cap;
+    long long ea = 0, eb = 0;
+    unsigned long long need = ~0ull;
+    if (fits) {
+        ea = up((long long)ea_u);
+        eb = up((long long)eb_u);
+        need = planes * ((unsigned long long)ea + (unsigned long long)eb) * sizeof(float);
+        fits = need <= kScratchBytes;
+    }
+    if (!fits) {
         fprintf(stderr,
-                "[zblas] zlift_sgemm_noalloc: %dx%dx%d needs %llu bytes of scratch; the fixed "
-                "array holds %zu\n", m, n, k, need, kScratchBytes);
+                "[zblas] zlift_sgemm_noalloc: %dx%dx%d needs more scratch than the fixed "
+                "array's %zu bytes\n", m, n, k, kScratchBytes);
         return CUBLAS_STATUS_INVALID_VALUE;
     }
     float* base = scratch_on_current_device();

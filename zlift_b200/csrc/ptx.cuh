@@ -24,9 +24,27 @@ enum DevError : int {
 
 static __device__ int g_dev_error = 0;
 
-// Limit for any single mbarrier wait, in nanoseconds.  Waits in these
-// kernels normally end within microseconds.
-constexpr unsigned long long kWaitLimitNs = 2000000000ull;
+// Limit for any single mbarrier or flag wait, in nanoseconds (default 2 s;
+// zlift_set_wait_limit_ns changes it for every kernel of the library on the
+// current device).  Waits in these kernels normally end within
+// microseconds.  One copy per translation unit, like g_dev_error.
+constexpr unsigned long long kDefaultWaitLimitNs = 2000000000ull;
+static __device__ unsigned long long g_wait_limit_ns = kDefaultWaitLimitNs;
+
+// Host side: sets this translation unit's copy of the wait limit on the
+// current device (each .cu file that includes this header exposes it
+// through its own named function).
+static inline int set_unit_wait_limit(unsigned long long ns) {
+    return cudaMemcpyToSymbol(g_wait_limit_ns, &ns, sizeof ns) == cudaSuccess ? 0 : 1;
+}
+static inline unsigned long long get_unit_wait_limit() {
+    unsigned long long ns = 0;
+    if (cudaMemcpyFromSymbol(&ns, g_wait_limit_ns, sizeof ns) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    return ns;
+}
 
 __device__ __forceinline__ unsigned long long globaltimer() {
     unsigned long long t;
@@ -80,10 +98,11 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity
 }
 
 // Wait until the barrier's phase with the given parity has completed.
-// Returns false (after recording the error and raising *abort) when the
-// time limit passes or another role of the CTA has already aborted.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
-                                          volatile int* abort) {
+// Returns false (after recording the error and raising *abort) when
+// `limit_ns` passes or another role of the CTA has already aborted.
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity,
+                                              volatile int* abort,
+                                              unsigned long long limit_ns) {
     const uint32_t a = smem_u32(bar);
     if (mbar_try_wait(a, parity)) return true;
     const unsigned long long t0 = globaltimer();
@@ -92,13 +111,21 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
         if (mbar_try_wait(a, parity)) return true;
         if ((++spins & 255u) == 0) {
             if (*abort) return false;
-            if (globaltimer() - t0 > kWaitLimitNs) {
+            if (globaltimer() - t0 > limit_ns) {
                 atomicCAS(&g_dev_error, 0, (int)kErrWaitTimeout);
                 *abort = 1;
                 return false;
             }
         }
     }
+}
+
+// mbar_wait_for with the library's limit (g_wait_limit_ns).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
+                                          volatile int* abort) {
+    const uint32_t a = smem_u32(bar);
+    if (mbar_try_wait(a, parity)) return true;
+    return mbar_wait_for(bar, parity, abort, g_wait_limit_ns);
 }
 
 // Count-based hand-off between threads of one CTA through a 32-bit word in
@@ -127,7 +154,7 @@ __device__ __forceinline__ bool flag_wait(uint32_t* flag, uint32_t target, volat
         if (flag_load_acquire(a) >= target) return true;
         if ((++spins & 63u) == 0) {
             if (*abort) return false;
-            if (globaltimer() - t0 > kWaitLimitNs) {
+            if (globaltimer() - t0 > g_wait_limit_ns) {
                 atomicCAS(&g_dev_error, 0, (int)kErrWaitTimeout);
                 *abort = 1;
                 return false;
@@ -294,6 +321,14 @@ __device__ __forceinline__ void tc_fence_after() {
 // tensor cores and TMA).
 __device__ __forceinline__ void fence_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Order generic-proxy global-memory accesses with async-proxy ones (bulk
+// copies, TMA) of this thread: global data written with ordinary stores by
+// another CTA, and acquired through an atomic, may then be read by a bulk
+// copy this thread issues.
+__device__ __forceinline__ void fence_async_global() {
+    asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 
 // D[tmem] (+)= A[smem desc] * B[smem desc]; kind::f16 (f16/bf16 inputs).

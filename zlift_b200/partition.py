@@ -29,6 +29,48 @@ def flash_pairs(block, elem: int, pair_begin: int, pair_end: int, stream=None) -
                                        pair_begin, pair_end, s)
 
 
+class PeerLost(RuntimeError):
+    """A rank did not announce the next step in time (it left the job)."""
+
+
+class Heartbeat:
+    """Host-side liveness check between steps of a multi-GPU job.
+
+    Before launching step `i`, every rank calls ``beat(i)``: it publishes
+    ``hb/<i>/<rank>`` in the job's key-value store and waits, up to
+    `timeout_s`, for every other rank's key of the same step.  A rank that
+    left the job between steps is seen here, on the host, before any kernel
+    or collective of step `i` is launched -- so no GPU ever waits on a peer
+    that is gone.  Raises PeerLost (with the missing ranks) on expiry.
+
+    The store is any torch.distributed Store (TCPStore, FileStore, ...).
+    """
+
+    def __init__(self, store, world: int, rank: int, timeout_s: float = 5.0):
+        self.store, self.world, self.rank = store, world, rank
+        self.timeout_s = timeout_s
+
+    def beat(self, step: int) -> None:
+        from datetime import timedelta
+        self.store.set(f"hb/{step}/{self.rank}", "1")
+        others = [f"hb/{step}/{r}" for r in range(self.world) if r != self.rank]
+        if not others:
+            return
+        try:
+            self.store.wait(others, timedelta(seconds=self.timeout_s))
+        except Exception as e:            # store timeout or a closed store
+            missing = []
+            for r in range(self.world):
+                if r == self.rank:
+                    continue
+                try:
+                    if not self.store.check([f"hb/{step}/{r}"]):
+                        missing.append(r)
+                except Exception:
+                    missing.append(r)
+            raise PeerLost(f"step {step}: no heartbeat from rank(s) {missing or '?'}") from e
+
+
 class Comm:
     """NCCL communicator of the partition layer."""
 
@@ -50,8 +92,15 @@ class Comm:
         return buf.raw
 
     def wait(self, stream, timeout_ms: int = 10000) -> int:
+        """Waits for `stream` with a deadline (zlift_part_comm_wait): 0 once
+        the stream's work is done; 200 past the deadline and 100 + NCCL's
+        code on an asynchronous NCCL error -- the library has then aborted
+        the communicator, which this object drops."""
         s = int(getattr(stream, "cuda_stream", stream or 0))
-        return self.lib.zlift_part_comm_wait(self.c, s, timeout_ms)
+        rc = self.lib.zlift_part_comm_wait(self.c, s, timeout_ms)
+        if rc >= 100:
+            self.c = None
+        return rc
 
     def close(self):
         if self.c:
