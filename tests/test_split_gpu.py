@@ -177,6 +177,10 @@ def test_split_cuda_graph_replays(handle, oracle_lib, cuda):
     g = torch.cuda.CUDAGraph()
     with torch.cuda.stream(s):
         handle.set_stream(s)
+        # one eager call on the capture stream first: a stream's K-split
+        # workspace is allocated on its first GEMM, never inside a capture
+        assert handle.gemm_ex(0, 0, m, n, k, 1.0, dA, 2, m, dB, 2, k, 0.0, dC, 2, m) == 0
+        s.synchronize()
         with torch.cuda.graph(g, stream=s):
             assert handle.gemm_ex(0, 0, m, n, k, 1.0, dA, 2, m, dB, 2, k, 0.0, dC, 2, m) == 0
     handle.set_stream(torch.cuda.current_stream())
