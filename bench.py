@@ -17,9 +17,12 @@ those of gemm_f16, the configuration the metric is quoted on, and
                      alpha=1/sqrt(512), beta=0; N>1: batch split across GPUs
                      (zlift_part_gemm_strided_batched_ex), no collective.
   gemm_i8            cublasGemmEx int8 -> int32, M=2048 K=4096 N=14336, TN;
-                     N>1: N-column split + NCCL all-gather of C
-                     (zlift_part_gemm_ex_nsplit); also reported without the
-                     gather as gemm_i8_nogather.
+                     N>1: N-column split with the NCCL all-gather of C
+                     overlapping the GEMM sub-block by sub-block
+                     (zlift_part_gemm_ex_nsplit_overlap); also reported with
+                     the gather after the whole GEMM (gemm_i8_serialgather,
+                     zlift_part_gemm_ex_nsplit) and without it
+                     (gemm_i8_nogather).
   fmha               flash forward bf16 B=8 H=32 S=4096 D=128 causal, fp32
                      LSE; N>1: (batch, head) pairs split across GPUs
                      (zlift_part_flash_fwd), no collective.
@@ -317,16 +320,32 @@ class GemmBF16Batched(Workload):
                 "torch.baddbmm bf16 (NVIDIA cuBLAS strided batched), same shape/alpha")
 
 
+def sub_blocks_for(n, world):
+    """Sub-blocks of the overlapped N-split: the most (of 4, 2) whose column
+    pieces stay multiples of 128, else 1."""
+    for sb in (4, 2):
+        if n % (world * sb * 128) == 0:
+            return sb
+    return 1
+
+
 class GemmI8(Workload):
     name, dtype, unit, scaling = "gemm_i8", "int8", "TOPS", "strong"
     peak_scale = 2.0
     M, K, N = 2048, 4096, 14336
     gather = True
+    overlap = True           # N > 1: all-gather overlapped with the GEMM, sub-block by sub-block
 
     @classmethod
     def config_for(cls, world):
-        par = (f"N-split x{world} + NCCL all-gather of C (zlift_part_gemm_ex_nsplit)"
-               if cls.gather else f"N-split x{world}, column blocks left on their GPUs")
+        if not cls.gather:
+            par = f"N-split x{world}, column blocks left on their GPUs"
+        elif cls.overlap and world > 1:
+            par = (f"N-split x{world} in {sub_blocks_for(cls.N, world)} sub-blocks, NCCL "
+                   f"all-gather of each overlapping the next GEMM "
+                   f"(zlift_part_gemm_ex_nsplit_overlap)")
+        else:
+            par = f"N-split x{world} + NCCL all-gather of C after the GEMM (zlift_part_gemm_ex_nsplit)"
         return {"workload": "cublasGemmEx int8->int32 M=2048 K=4096 N=14336 transa=T transb=N "
                             "alpha=1 beta=0", "m": 2048, "n": 14336, "k": 4096,
                 "inputs": "A,B uniform integers in [-127,127] (seeded)",
@@ -357,7 +376,12 @@ class GemmI8(Workload):
 
     def step(self, i):
         from zlift_b200 import partition
-        if self.gather:
+        if self.gather and self.overlap and self.world > 1:
+            st = partition.gemm_ex_nsplit_overlap(
+                self.h, self.comm, self.world, self.rank, sub_blocks_for(self.N, self.world), 1,
+                0, self.M, self.N, self.K, 1, self.A, 3, self.K, self.B, 3, self.K, 0, self.C,
+                10, 72)
+        elif self.gather:
             st = partition.gemm_ex_nsplit(self.h, self.comm, self.world, self.rank, 1, 0, self.M,
                                           self.N, self.K, 1, self.A, 3, self.K, self.B, 3,
                                           self.K, 0, self.C, 10, 72)
@@ -396,6 +420,11 @@ class GemmI8(Workload):
 class GemmI8NoGather(GemmI8):
     name = "gemm_i8_nogather"
     gather = False
+
+
+class GemmI8SerialGather(GemmI8):
+    name = "gemm_i8_serialgather"
+    overlap = False
 
 
 class Fmha(Workload):
@@ -523,7 +552,8 @@ class Sgemm(Workload):
         return run, "torch.mm fp32, TF32 off (NVIDIA cuBLAS)"
 
 
-WORKLOADS = {w.name: w for w in (GemmF16, GemmBF16Batched, GemmI8, GemmI8NoGather, Fmha, Sgemm)}
+WORKLOADS = {w.name: w for w in (GemmF16, GemmBF16Batched, GemmI8, GemmI8NoGather,
+                                 GemmI8SerialGather, Fmha, Sgemm)}
 
 
 # --------------------------------------------------------------------------
@@ -775,7 +805,8 @@ def run_workload(W, h, dev, rank, world, local, stream, steps, warmup, clk, pk, 
                          "traffic": traffic_from_profile(w.name) if world == 1 else None,
                          "kernel_ms": kernel_ms,
                          "kernel": "per-step CUDA events around each call"
-                                   + (" (GEMM + NCCL all-gather)" if (w.name == "gemm_i8" and world > 1)
+                                   + (" (GEMM + NCCL all-gather)"
+                                      if (w.name.startswith("gemm_i8") and w.gather and world > 1)
                                       else "")},
             "e2e": {"value": w.flops / (e2e_ms * 1e-3) / 1e12, "unit": w.unit,
                     "h2d_bytes_per_step": bi, "d2h_bytes_per_step": bo, "ms_per_step": e2e_ms},
@@ -812,8 +843,8 @@ def main(argv=None):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     names = ORDER if a.workload == "all" else [a.workload]
-    if a.workload == "all" and world > 1:
-        names = names + ["gemm_i8_nogather"]
+    if a.workload == "all" and max(world, a.gpus) > 1:
+        names = names + ["gemm_i8_serialgather", "gemm_i8_nogather"]
     head = HEADLINE if HEADLINE in names else names[0]
 
     if a.impl == "reference":

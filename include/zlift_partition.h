@@ -65,6 +65,34 @@ ZLIFT_API int zlift_part_gemm_ex_nsplit(
     int k, const void *alpha, const void *A, int Atype, int lda, const void *B_block,
     int Btype, int ldb, const void *beta, void *C, int Ctype, int computeType);
 
+/* Column ownership of the overlapped N-split: the n columns form
+ * `sub_blocks` super-blocks of n / sub_blocks columns each, and within each
+ * super-block rank r owns the r-th of nranks equal pieces of
+ * w = n / (sub_blocks * nranks) columns.  Writes the global columns
+ * [begin, end) of rank `rank`'s sub-block `s`.  Returns 1 on bad arguments
+ * or when w is not a whole number. */
+ZLIFT_API int zlift_part_nsplit_cols(long long n, int nranks, int rank, int sub_blocks, int s,
+                                     long long *begin, long long *end);
+
+/* N-split GEMM whose all-gather overlaps the GEMM.  Extends cublasGemmEx
+ * (zblas/zblas.c:357-391) across GPUs, like zlift_part_gemm_ex_nsplit, but
+ * with the interleaved column ownership of zlift_part_nsplit_cols:
+ * `B_cols` holds this rank's sub-blocks of op(B) back to back (sub-block s
+ * = the w columns zlift_part_nsplit_cols gives for s; transb = N:
+ * k x (sub_blocks * w), leading dim ldb).  The GEMM of each sub-block runs
+ * on the handle's stream (using all SMs but ZLIFT_PART_COMM_SMS, default
+ * 16, so NCCL's kernels run next to it); each super-block's in-place
+ * ncclAllGather runs on a second stream of the communicator as soon as
+ * this rank's GEMM of it is done, overlapping the next sub-block's GEMM.
+ * The handle's stream waits for the last gather: C (m x n, leading dim m)
+ * is complete there, as with zlift_part_gemm_ex_nsplit.  Every rank calls
+ * it with the same sizes and sub_blocks. */
+ZLIFT_API int zlift_part_gemm_ex_nsplit_overlap(
+    void *handle, void *comm, int nranks, int rank, int sub_blocks, int transa, int transb,
+    int m, int n, int k, const void *alpha, const void *A, int Atype, int lda,
+    const void *B_cols, int Btype, int ldb, const void *beta, void *C, int Ctype,
+    int computeType);
+
 /* Attention forward restricted to (batch, head) pairs [pair_begin,
  * pair_end) in batch-major order, on `stream` (parameter block as for
  * zlift_flash_fwd).  0 done, 1 declined, 2 launch failure. */

@@ -220,3 +220,26 @@ def test_sgemm_strided_batched(handle, oracle_lib):
         assert normwise(g, r) <= 1e-5, b
         # the padding between matrices is left alone
         assert np.array_equal(got[b * sC + m * n:(b + 1) * sC], ref[b * sC + m * n:(b + 1) * sC])
+
+
+def test_nsplit_overlap_one_rank_equals_one_shot(handle):
+    """The overlapped N-split on one rank (no communicator): four sub-block
+    GEMMs into their columns of C give the one-shot int8 product's bits."""
+    import torch
+    from zlift_b200 import blas, inputs, partition
+    M, K, N = 512, 1024, 2048
+    A = to_dev(inputs.make("i8", "int8", 401, K * M), "i8")
+    Bh = inputs.make("i8", "int8", 402, K * N)
+    B = to_dev(Bh, "i8")
+    one = torch.zeros(N * M, dtype=torch.int32, device="cuda")
+    assert handle.gemm_ex(1, 0, M, N, K, 1, A, 3, K, B, 3, K, 0, one, 10, M,
+                          compute=blas.COMPUTE_32I) == 0
+    SB = 4
+    cols = [partition.nsplit_cols(N, 1, 0, SB, s) for s in range(SB)]
+    Bcols = torch.cat([B[b * K:e * K] for b, e in cols])
+    got = torch.full((N * M,), -1, dtype=torch.int32, device="cuda")
+    assert partition.gemm_ex_nsplit_overlap(handle, None, 1, 0, SB, 1, 0, M, N, K, 1, A, 3, K,
+                                            Bcols, 3, K, 0, got, 10, 72) == 0
+    torch.cuda.synchronize()
+    assert blas.device_error() == 0
+    assert torch.equal(one, got)

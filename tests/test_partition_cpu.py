@@ -118,3 +118,30 @@ def test_pair_split_covers_every_batch_head_once_gloo(built_lib):
     out = mgr.dict()
     mp.spawn(_pair_worker, args=(world, port, out), nprocs=world, join=True)
     assert dict(out) == {0: True, 1: True}
+
+
+@pytest.mark.parametrize("n,nranks,sb", [(14336, 2, 4), (14336, 4, 4), (14336, 8, 2), (4096, 2, 4),
+                                         (384, 3, 1), (64, 8, 8)])
+def test_nsplit_cols_cover_every_column_once(built_lib, n, nranks, sb):
+    """Overlapped N-split ownership: super-block s holds every rank's
+    sub-block s in rank order, so each super-block is one in-place
+    all-gather, and the union over ranks and sub-blocks is every column."""
+    from zlift_b200 import partition
+    owner = np.full(n, -1)
+    for s in range(sb):
+        prev = s * (n // sb)
+        for r in range(nranks):
+            b, e = partition.nsplit_cols(n, nranks, r, sb, s)
+            assert b == prev and e - b == n // (sb * nranks)
+            assert np.all(owner[b:e] == -1)
+            owner[b:e] = r
+            prev = e
+        assert prev == (s + 1) * (n // sb)
+    assert np.all(owner >= 0)
+
+
+def test_nsplit_cols_rejects_uneven(built_lib):
+    from zlift_b200 import partition
+    for args in ((100, 3, 1, 1, 0), (14338, 8, 0, 4, 0), (10, 2, 2, 1, 0), (10, 2, 0, 1, 1)):
+        with pytest.raises(ValueError):
+            partition.nsplit_cols(*args)

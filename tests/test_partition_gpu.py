@@ -3,8 +3,9 @@
 One process per GPU (spawned here), NCCL communicator created by the
 library (zlift_part_unique_id / zlift_part_comm_init; the id travels over a
 gloo process group):
-  - int8 N-split GEMM + all-gather: every rank's gathered C equals the
-    single-GPU product bit for bit;
+  - int8 N-split GEMM + all-gather, with the gather after the GEMM and
+    overlapped with it sub-block by sub-block: every rank's gathered C
+    equals the single-GPU product bit for bit;
   - flash forward split by (batch, head) pairs: each rank's pairs equal the
     single-GPU result bit for bit (same kernel, same tiles).
 """
@@ -67,6 +68,17 @@ def _worker(rank, world, port, out):
         assert h.gemm_ex(1, 0, M, N, K, 1, A, 3, K, Bfull, 3, K, 0, ref, 10, M, compute=72) == 0
         torch.cuda.synchronize()
         ok_gemm = bool(torch.equal(C, ref))
+        # ---- int8 N-split with the gather overlapped, 4 sub-blocks ----
+        SB = 4
+        cols = [partition.nsplit_cols(N, world, rank, SB, s) for s in range(SB)]
+        Bcols = torch.cat([Bfull[b:e] for b, e in cols]).contiguous()
+        C2 = torch.full((N, M), -1, dtype=torch.int32, device="cuda")
+        st = partition.gemm_ex_nsplit_overlap(h, comm, world, rank, SB, 1, 0, M, N, K, 1, A, 3,
+                                              K, Bcols, 3, K, 0, C2, 10, 72)
+        assert st == 0, st
+        assert comm.wait(stream, 30000) == 0
+        torch.cuda.synchronize()
+        ok_gemm = ok_gemm and bool(torch.equal(C2, ref))
         # ---- attention split by (batch, head) ----
         Bq, S, H, D = 2, 512, 4, 128
         q = torch.randn(Bq, S, H, D, generator=g, device="cuda").bfloat16()

@@ -84,6 +84,12 @@ SIGNATURES = [
                                           c_int, c_int, c_void_p, c_void_p, c_int, c_int,
                                           c_void_p, c_int, c_int, c_void_p, c_void_p, c_int,
                                           c_int]),
+    ("zlift_part_nsplit_cols", c_int, [c_ll, c_int, c_int, c_int, c_int, ctypes.POINTER(c_ll),
+                                       ctypes.POINTER(c_ll)]),
+    ("zlift_part_gemm_ex_nsplit_overlap", c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int,
+                                                  c_int, c_int, c_int, c_int, c_void_p, c_void_p,
+                                                  c_int, c_int, c_void_p, c_int, c_int, c_void_p,
+                                                  c_void_p, c_int, c_int]),
     ("zlift_part_flash_fwd", c_int, [c_void_p, c_uint, c_int, c_ll, c_ll, c_void_p]),
 ]
 

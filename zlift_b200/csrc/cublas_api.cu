@@ -159,6 +159,7 @@ static void attach_split_ws(Handle* h, GemmDesc& d, cudaStream_t s) {
 // the layout is outside what TMA can describe.
 static cublasStatus_t run_gemm(Handle* h, GemmDesc& d, cudaStream_t s) {
     if (d.m == 0 || d.n == 0 || d.batch == 0) return CUBLAS_STATUS_SUCCESS;
+    d.sm_limit = h->sm_target;
     if (d.k == 0) return map_launch(gemm_simt(d, s));   // C = beta*C
     if (d.kind == Kind::TF32X3 || d.kind == Kind::TF32) {
         // tf32 planes of A and B in scratch, K-major with 16-byte rows:

@@ -60,6 +60,9 @@ struct GemmDesc {
     size_t split_work_bytes = 0;
     unsigned long long* split_counters = nullptr;
     unsigned long long split_epoch = 0;
+    // Most SMs the persistent kernel may occupy (0 = all; cublasSetSmCountTarget),
+    // e.g. to leave SMs to a collective that runs at the same time.
+    int sm_limit = 0;
 };
 
 enum EpiFlags : int { kEpiBias = 1, kEpiRelu = 2, kEpiGelu = 4 };

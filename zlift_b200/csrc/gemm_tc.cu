@@ -31,6 +31,7 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cstdio>
 #include <cstdlib>
@@ -1014,6 +1015,7 @@ struct Maps {
     CUtensorMap a, b, a2, b2, c;
     bool staged;            // C described by `c`: TMA-staged epilogue
     bool pair;              // CTA-pair (cta_group::2) kernel, 256-row tiles
+    int sm_limit;           // most SMs to occupy (0 = all)
 };
 
 // Kinds and widths the CTA-pair kernel is built for.
@@ -1096,8 +1098,9 @@ int launch_one(const Maps& m, const TcParams& p, cudaStream_t s) {
         }
         attr_set.fetch_or(bit);
     }
-    const int slots = PAIR ? (max_clusters[dev & 63] > 0 ? max_clusters[dev & 63] : num_sms() / 2)
-                           : num_sms();
+    int slots = PAIR ? (max_clusters[dev & 63] > 0 ? max_clusters[dev & 63] : num_sms() / 2)
+                     : num_sms();
+    if (m.sm_limit > 0) slots = std::min(slots, PAIR ? std::max(1, m.sm_limit / 2) : m.sm_limit);
     TcParams q = p;
     const int tiles = p.tiles_m * p.tiles_n * p.batch;
     split_tail(q, tiles, slots, m.staged ? BN * BM * 4 * (PAIR ? 2 : 1) : 0,
@@ -1207,9 +1210,10 @@ int gemm_tc(const GemmDesc& d, cudaStream_t s) {
     // 256x256 tiles 1.00, single 128x256 0.90, single 128x128 0.69).  Pairs
     // need K >= 2048 bytes (short K: the pair's extra synchronisation
     // outweighs the halved B loads).  fp32 forms: 128 (or 64) wide tiles.
-    const int sms = num_sms();
+    const int sms = d.sm_limit > 0 ? std::min(num_sms(), std::max(2, d.sm_limit)) : num_sms();
     Maps maps;
     maps.pair = false;
+    maps.sm_limit = d.sm_limit > 0 ? sms : 0;
     int BN = 128;
     if (d.kind == Kind::TF32X3 || d.kind == Kind::TF32) {
         const long long tiles256 = (long long)((d.m + BM - 1) / BM) * ((d.n + 255) / 256) * d.batch;

@@ -15,8 +15,10 @@
 #include <chrono>
 #include <cstdlib>
 #include <cstring>
+#include <map>
 #include <mutex>
 #include <thread>
+#include <vector>
 
 namespace {
 
@@ -74,6 +76,59 @@ int elem_size(int t) {
     }
 }
 
+// Per-communicator resources of the overlapped N-split: a second stream for
+// the collectives and one event per sub-block (GEMM of sub-block s done on
+// the handle's stream), plus the event the handle's stream waits on at the
+// end.  Created on first use, released by zlift_part_comm_destroy.
+struct Overlap {
+    int device = -1;
+    cudaStream_t stream = nullptr;
+    std::vector<cudaEvent_t> gemm_done;
+    cudaEvent_t gathered = nullptr;
+};
+std::mutex g_overlap_mu;
+std::map<void*, Overlap> g_overlap;
+
+Overlap* overlap_for(void* comm, int sub_blocks) {
+    std::lock_guard<std::mutex> lock(g_overlap_mu);
+    Overlap& o = g_overlap[comm];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!o.stream) {
+        if (cudaStreamCreateWithFlags(&o.stream, cudaStreamNonBlocking) != cudaSuccess ||
+            cudaEventCreateWithFlags(&o.gathered, cudaEventDisableTiming) != cudaSuccess) {
+            cudaGetLastError();
+            g_overlap.erase(comm);
+            return nullptr;
+        }
+        o.device = dev;
+    }
+    if (o.device != dev) return nullptr;
+    while ((int)o.gemm_done.size() < sub_blocks) {
+        cudaEvent_t e;
+        if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) {
+            cudaGetLastError();
+            return nullptr;
+        }
+        o.gemm_done.push_back(e);
+    }
+    return &o;
+}
+
+void release_overlap(void* comm) {
+    std::lock_guard<std::mutex> lock(g_overlap_mu);
+    auto it = g_overlap.find(comm);
+    if (it == g_overlap.end()) return;
+    int cur = 0;
+    cudaGetDevice(&cur);
+    cudaSetDevice(it->second.device);
+    for (cudaEvent_t e : it->second.gemm_done) cudaEventDestroy(e);
+    if (it->second.gathered) cudaEventDestroy(it->second.gathered);
+    if (it->second.stream) cudaStreamDestroy(it->second.stream);
+    cudaSetDevice(cur);
+    g_overlap.erase(it);
+}
+
 }  // namespace
 
 extern "C" {
@@ -120,6 +175,7 @@ int zlift_part_comm_init(void** comm, int nranks, int rank, const void* id128) {
 int zlift_part_comm_destroy(void* comm) {
     const Nccl& n = nccl();
     if (!n.ok || !comm) return 1;
+    release_overlap(comm);
     NcclResult r = n.comm_destroy(comm);
     return r == kNcclSuccess ? 0 : 100 + r;
 }
@@ -136,12 +192,14 @@ int zlift_part_comm_wait(void* comm, void* stream, int timeout_ms) {
         n.comm_get_async_error(comm, &err);
         if (err != kNcclSuccess && err != kNcclInProgress) {
             n.comm_abort(comm);
+            release_overlap(comm);
             return 100 + err;
         }
         const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(
                             std::chrono::steady_clock::now() - t0).count();
         if (ms > timeout_ms) {
             n.comm_abort(comm);
+            release_overlap(comm);
             return 200;
         }
         std::this_thread::sleep_for(std::chrono::microseconds(200));
@@ -213,6 +271,95 @@ int zlift_part_gemm_ex_nsplit(void* handle, void* comm, int nranks, int rank, in
         if (r == kNcclSuccess) r = r2;
     }
     return r == kNcclSuccess ? 0 : 100 + r;
+}
+
+int zlift_part_nsplit_cols(long long n, int nranks, int rank, int sub_blocks, int s,
+                           long long* begin, long long* end) {
+    if (!begin || !end || n <= 0 || nranks <= 0 || rank < 0 || rank >= nranks || sub_blocks <= 0 ||
+        s < 0 || s >= sub_blocks)
+        return 1;
+    const long long pieces = (long long)nranks * sub_blocks;
+    if (n % pieces) return 1;
+    const long long w = n / pieces;
+    *begin = (long long)s * (n / sub_blocks) + (long long)rank * w;
+    *end = *begin + w;
+    return 0;
+}
+
+int zlift_part_gemm_ex_nsplit_overlap(void* handle, void* comm, int nranks, int rank,
+                                      int sub_blocks, int transa, int transb, int m, int n,
+                                      int k, const void* alpha, const void* A, int Atype,
+                                      int lda, const void* B_cols, int Btype, int ldb,
+                                      const void* beta, void* C, int Ctype, int computeType) {
+    if (nranks <= 0 || rank < 0 || rank >= nranks || m < 0 || n <= 0 || sub_blocks <= 0 ||
+        sub_blocks > 64)
+        return 1;
+    long long c0, c1;
+    if (zlift_part_nsplit_cols(n, nranks, rank, sub_blocks, 0, &c0, &c1)) return 1;
+    const long long w = c1 - c0;
+    const int es = elem_size(Ctype);
+    const int bes = elem_size(Btype);
+    // sub-block s of op(B) in B_cols: w columns; transb = N: columns are
+    // ldb apart, transb = T: rows of the stored matrix are adjacent
+    const long long b_step = transb == 0 ? w * (long long)ldb : w;
+    void* sv = nullptr;
+    cublasGetStream_v2(handle, &sv);
+    cudaStream_t s = static_cast<cudaStream_t>(sv);
+    if (nranks == 1) {
+        for (int sb = 0; sb < sub_blocks; sb++) {
+            zlift_part_nsplit_cols(n, 1, 0, sub_blocks, sb, &c0, &c1);
+            const int st = cublasGemmEx(handle, transa, transb, m, (int)w, k, alpha, A, Atype,
+                                        lda, static_cast<const char*>(B_cols) + sb * b_step * bes,
+                                        Btype, ldb, beta,
+                                        static_cast<char*>(C) + c0 * (long long)m * es, Ctype, m,
+                                        computeType, 0);
+            if (st) return st;
+        }
+        return 0;
+    }
+    const Nccl& nc = nccl();
+    if (!nc.ok || !comm) return 1;
+    Overlap* ov = overlap_for(comm, sub_blocks);
+    if (!ov) return 1;
+    // leave SMs to NCCL's kernels, which run next to the GEMMs
+    int target = 0;
+    cublasGetSmCountTarget(handle, &target);
+    int reserve = 16;
+    if (const char* e = getenv("ZLIFT_PART_COMM_SMS")) reserve = atoi(e);
+    const int sms = zl::num_sms();
+    if (reserve > 0 && reserve < sms) cublasSetSmCountTarget(handle, sms - reserve);
+    const int dt = Ctype == zl::kR32I ? kNcclInt32 : kNcclInt8;
+    const size_t unit = Ctype == zl::kR32I ? 1 : (size_t)es;
+    int rc = 0;
+    for (int sb = 0; sb < sub_blocks && rc == 0; sb++) {
+        zlift_part_nsplit_cols(n, nranks, rank, sub_blocks, sb, &c0, &c1);
+        char* mine = static_cast<char*>(C) + c0 * (long long)m * es;
+        rc = cublasGemmEx(handle, transa, transb, m, (int)w, k, alpha, A, Atype, lda,
+                          static_cast<const char*>(B_cols) + sb * b_step * bes, Btype, ldb, beta,
+                          mine, Ctype, m, computeType, 0);
+        if (rc) break;
+        // the gather of super-block sb (every rank's sub-block sb, in rank
+        // order, in place) waits only for this GEMM on this rank; NCCL pairs
+        // it with the same gather on the other ranks
+        if (cudaEventRecord(ov->gemm_done[sb], s) != cudaSuccess ||
+            cudaStreamWaitEvent(ov->stream, ov->gemm_done[sb], 0) != cudaSuccess) {
+            cudaGetLastError();
+            rc = 13;
+            break;
+        }
+        char* super = static_cast<char*>(C) + (long long)sb * (n / sub_blocks) * m * es;
+        NcclResult r = nc.all_gather(mine, super, (size_t)w * (size_t)m * unit, dt, comm,
+                                     ov->stream);
+        if (r != kNcclSuccess) rc = 100 + r;
+    }
+    cublasSetSmCountTarget(handle, target);
+    // the handle's stream continues once the last gather has landed
+    if (cudaEventRecord(ov->gathered, ov->stream) != cudaSuccess ||
+        cudaStreamWaitEvent(s, ov->gathered, 0) != cudaSuccess) {
+        cudaGetLastError();
+        if (rc == 0) rc = 13;
+    }
+    return rc;
 }
 
 int zlift_part_flash_fwd(const void* params, unsigned bytes, int elem, long long pair_begin,

@@ -132,3 +132,29 @@ def gemm_strided_batched_range(handle, batch_begin, batch_end, transa, transb, m
         handle.h, batch_begin, batch_end, transa, transb, m, n, k, ctypes.byref(al), _ptr(A),
         Atype, lda, sA, _ptr(B), Btype, ldb, sB, ctypes.byref(be), _ptr(C), Ctype, ldc, sC,
         compute)
+
+
+def nsplit_cols(n: int, nranks: int, rank: int, sub_blocks: int, s: int) -> tuple[int, int]:
+    """Global columns [begin, end) of `rank`'s sub-block `s` in the
+    overlapped N-split (zlift_part_nsplit_cols)."""
+    b, e = ctypes.c_longlong(), ctypes.c_longlong()
+    rc = load().zlift_part_nsplit_cols(n, nranks, rank, sub_blocks, s, ctypes.byref(b),
+                                       ctypes.byref(e))
+    if rc:
+        raise ValueError(f"zlift_part_nsplit_cols({n}, {nranks}, {rank}, {sub_blocks}, {s})")
+    return b.value, e.value
+
+
+def gemm_ex_nsplit_overlap(handle, comm, nranks, rank, sub_blocks, transa, transb, m, n, k,
+                           alpha, A, Atype, lda, B_cols, Btype, ldb, beta, C, Ctype,
+                           compute) -> int:
+    """N-split GEMM with its all-gather overlapped, sub-block by sub-block
+    (zlift_part_gemm_ex_nsplit_overlap)."""
+    from .blas import COMPUTE_32I, R_32I, _ptr
+    integer = compute in (COMPUTE_32I, R_32I)
+    al = ctypes.c_int32(int(alpha)) if integer else ctypes.c_float(float(alpha))
+    be = ctypes.c_int32(int(beta)) if integer else ctypes.c_float(float(beta))
+    return load().zlift_part_gemm_ex_nsplit_overlap(
+        handle.h, comm.c if comm is not None else None, nranks, rank, sub_blocks, transa,
+        transb, m, n, k, ctypes.byref(al), _ptr(A), Atype, lda, _ptr(B_cols), Btype, ldb,
+        ctypes.byref(be), _ptr(C), Ctype, compute)
