@@ -346,36 +346,55 @@ __device__ __forceinline__ void store_out(void* C, long long at, uint32_t raw, u
 
 // alpha * acc (+ beta * C already in the staging buffer) (+ bias, act),
 // converted in place: this thread's row of one 32-column staging chunk
-// ([column][row], 128 rows).
-template <int OUT>
-__device__ __forceinline__ void convert_chunk(const uint32_t (&v)[32], uint8_t* sbuf, int row,
-                                              float alpha, float beta, int32_t ia, int32_t ib,
-                                              bool use_beta, int epi, float bias_row) {
+// ([column][row], 128 rows).  BETA and ACT are compile-time so that each
+// loop body holds only the arithmetic it runs: with run-time flags inside
+// the unrolled loop the compiler predicated the activation (tanhf) for
+// every element, which made this conversion cost ~1250 clocks per chunk.
+template <int OUT, bool BETA, bool ACT>
+__device__ __forceinline__ void convert_chunk_t(const uint32_t (&v)[32], uint8_t* sbuf, int row,
+                                                float alpha, float beta, int32_t ia, int32_t ib,
+                                                int epi, float bias_row) {
     constexpr int ES = out_es(OUT);
 #pragma unroll
     for (int j = 0; j < 32; j++) {
         uint8_t* e = sbuf + (j * BM + row) * ES;
         if constexpr (OUT == kR32I) {
             uint32_t x = (uint32_t)ia * v[j];
-            if (use_beta) x += (uint32_t)ib * *reinterpret_cast<uint32_t*>(e);
+            if constexpr (BETA) x += (uint32_t)ib * *reinterpret_cast<uint32_t*>(e);
             *reinterpret_cast<uint32_t*>(e) = x;
-        } else if constexpr (OUT == kR32F) {
-            float x = alpha * __uint_as_float(v[j]);
-            if (use_beta) x = fmaf(beta, *reinterpret_cast<float*>(e), x);
-            if (epi) x = apply_act(x + bias_row, epi);
-            *reinterpret_cast<float*>(e) = x;
-        } else if constexpr (OUT == kR16F) {
-            float x = alpha * __uint_as_float(v[j]);
-            if (use_beta) x = fmaf(beta, __half2float(*reinterpret_cast<__half*>(e)), x);
-            if (epi) x = apply_act(x + bias_row, epi);
-            *reinterpret_cast<__half*>(e) = __float2half_rn(x);
         } else {
             float x = alpha * __uint_as_float(v[j]);
-            if (use_beta)
-                x = fmaf(beta, __bfloat162float(*reinterpret_cast<__nv_bfloat16*>(e)), x);
-            if (epi) x = apply_act(x + bias_row, epi);
-            *reinterpret_cast<__nv_bfloat16*>(e) = __float2bfloat16_rn(x);
+            if constexpr (OUT == kR32F) {
+                if constexpr (BETA) x = fmaf(beta, *reinterpret_cast<float*>(e), x);
+                if constexpr (ACT) x = apply_act(x + bias_row, epi);
+                *reinterpret_cast<float*>(e) = x;
+            } else if constexpr (OUT == kR16F) {
+                if constexpr (BETA) x = fmaf(beta, __half2float(*reinterpret_cast<__half*>(e)), x);
+                if constexpr (ACT) x = apply_act(x + bias_row, epi);
+                *reinterpret_cast<__half*>(e) = __float2half_rn(x);
+            } else {
+                if constexpr (BETA)
+                    x = fmaf(beta, __bfloat162float(*reinterpret_cast<__nv_bfloat16*>(e)), x);
+                if constexpr (ACT) x = apply_act(x + bias_row, epi);
+                *reinterpret_cast<__nv_bfloat16*>(e) = __float2bfloat16_rn(x);
+            }
         }
+    }
+}
+
+template <int OUT>
+__device__ __forceinline__ void convert_chunk(const uint32_t (&v)[32], uint8_t* sbuf, int row,
+                                              float alpha, float beta, int32_t ia, int32_t ib,
+                                              bool use_beta, int epi, float bias_row) {
+    if constexpr (OUT == kR32I) {
+        if (use_beta) convert_chunk_t<OUT, true, false>(v, sbuf, row, alpha, beta, ia, ib, 0, 0.f);
+        else convert_chunk_t<OUT, false, false>(v, sbuf, row, alpha, beta, ia, ib, 0, 0.f);
+    } else if (epi) {
+        if (use_beta) convert_chunk_t<OUT, true, true>(v, sbuf, row, alpha, beta, ia, ib, epi, bias_row);
+        else convert_chunk_t<OUT, false, true>(v, sbuf, row, alpha, beta, ia, ib, epi, bias_row);
+    } else {
+        if (use_beta) convert_chunk_t<OUT, true, false>(v, sbuf, row, alpha, beta, ia, ib, 0, 0.f);
+        else convert_chunk_t<OUT, false, false>(v, sbuf, row, alpha, beta, ia, ib, 0, 0.f);
     }
 }
 
@@ -894,13 +913,23 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                     tmem_ld32(taddr + c0, v);
                     if (c0 + 32 < BN) fetch(c0 + 32, old_next);
                     tmem_wait_ld();
-                    if (row_ok) {
+                    // the activation branch outside the unrolled loop (see
+                    // convert_chunk_t): epi == 0 compiles to no activation code
+                    if (row_ok && p.epi) {
 #pragma unroll
                         for (int j = 0; j < 32; j++) {
                             const int col = n0 + c0 + j;
                             if (col < p.n)
                                 store_out<OUT>(p.C, base + (long long)col * p.ldc, v[j], old[j],
                                                use_beta, alpha, beta, ia, ib, p.epi, bias_row);
+                        }
+                    } else if (row_ok) {
+#pragma unroll
+                        for (int j = 0; j < 32; j++) {
+                            const int col = n0 + c0 + j;
+                            if (col < p.n)
+                                store_out<OUT>(p.C, base + (long long)col * p.ldc, v[j], old[j],
+                                               use_beta, alpha, beta, ia, ib, 0, 0.f);
                         }
                     }
 #pragma unroll
