@@ -43,7 +43,7 @@ class AttnDesc(ctypes.Structure):
                 ("vb", _ll), ("vh", _ll), ("vr", _ll), ("ob", _ll), ("oh", _ll), ("orr", _ll),
                 ("batch", _int), ("heads", _int), ("kv_ratio", _int), ("sq", _int),
                 ("sk", _int), ("d", _int), ("scale", _f), ("causal", _int), ("diag", _int),
-                ("elem", _int)]
+                ("elem", _int), ("bias", _vp), ("bb", _ll), ("bh", _ll), ("br", _ll)]
 
 
 _oracle = None
@@ -187,23 +187,25 @@ def ref_gemm_strided_batched_ex(transa, transb, m, n, k, alpha, A, Atype, lda, s
     return rc
 
 
-def attention(q, k, v, causal, scale, elem, kv_ratio=1, diag=None, want_lse=True):
+def attention(q, k, v, causal, scale, elem, kv_ratio=1, diag=None, want_lse=True, bias=None):
     """Oracle attention on host arrays laid out [B, S, H, D] (16-bit values
-    as uint16 bit patterns, fp32 as float32).  Returns (O, LSE[B, H, Sq])."""
+    as uint16 bit patterns, fp32 as float32).  `bias`, if given, is an array
+    [B, H, Sq, Sk] of the input type added to the scaled scores.  Returns
+    (O, LSE[B, H, Sq])."""
     B, Sq, H, D = q.shape
     Sk = k.shape[1]
     o = np.zeros_like(q)
     lse = np.zeros((B, H, Sq), dtype=np.float32)
-    d = _desc(q, k, v, o, lse if want_lse else None, causal, scale, elem, kv_ratio, diag)
+    d = _desc(q, k, v, o, lse if want_lse else None, causal, scale, elem, kv_ratio, diag, bias)
     rc = oracle().zo_attention(ctypes.byref(d))
     assert rc == 0
     return o, lse
 
 
-def attention_rows(q, k, v, causal, scale, elem, bs, hs, is_, kv_ratio=1, diag=None):
+def attention_rows(q, k, v, causal, scale, elem, bs, hs, is_, kv_ratio=1, diag=None, bias=None):
     """fp64 O rows and LSE values for selected (b, h, i) query rows."""
     D = q.shape[3]
-    d = _desc(q, k, v, None, None, causal, scale, elem, kv_ratio, diag)
+    d = _desc(q, k, v, None, None, causal, scale, elem, kv_ratio, diag, bias)
     bs = np.ascontiguousarray(bs, dtype=np.int32)
     hs = np.ascontiguousarray(hs, dtype=np.int32)
     is_ = np.ascontiguousarray(is_, dtype=np.int32)
@@ -215,7 +217,7 @@ def attention_rows(q, k, v, causal, scale, elem, bs, hs, is_, kv_ratio=1, diag=N
     return o, l
 
 
-def _desc(q, k, v, o, lse, causal, scale, elem, kv_ratio, diag):
+def _desc(q, k, v, o, lse, causal, scale, elem, kv_ratio, diag, bias=None):
     B, Sq, H, D = q.shape
     Sk = k.shape[1]
     d = AttnDesc()
@@ -233,6 +235,10 @@ def _desc(q, k, v, o, lse, causal, scale, elem, kv_ratio, diag):
     d.causal = 1 if causal else 0
     d.diag = (Sk - Sq) if diag is None else diag
     d.elem = elem
+    if bias is not None:
+        assert bias.shape == (B, H, Sq, Sk) and bias.dtype == q.dtype
+        d.bias = _p(bias)
+        d.bb, d.bh, d.br = (s // bias.itemsize for s in bias.strides[:3])
     return d
 
 

@@ -28,7 +28,8 @@
  *       GELU pass, zblas/zblas.c:692-710 with gelu_tanh :638-642.
  *   zo_attention / zo_attention_rows      the fp32 math of fmha_f32
  *       (zblas/zblas_gpu.cpp:793-844) with the masking and rounding points
- *       of fmha_run (zblas/zblas_gpu.cpp:892-1039): causal mask
+ *       of fmha_run (zblas/zblas_gpu.cpp:892-1039): an optional additive
+ *       bias after the scaling (:963-966, :822-823), causal mask
  *       `key > query + diag` (:967), fully-masked rows give O = 0 (:981,
  *       :991, :1015), P rounded to the input type before P.V (:1001, via
  *       joint_matrix_copy), O accumulated wide and rounded once (:1013-1023).
@@ -412,6 +413,8 @@ typedef struct {
     float scale;
     int causal, diag;
     int elem;                      /* 0 = f16, 1 = bf16, 2 = f32 */
+    const void *bias;              /* additive bias of the input type, may be NULL */
+    int64_t bb, bh, br;            /* bias strides (elements) */
 } zo_attn_desc;
 
 static double ld_in(const void *p, int elem, int64_t at) {
@@ -449,6 +452,10 @@ static void attn_row(const zo_attn_desc *p, int b, int h, int i,
             s += ld_in(p->q, p->elem, qoff + t)
                * ld_in(p->k, p->elem, koff + (int64_t)j * p->kr + t);
         s *= (double)p->scale;
+        /* bias added after scaling, before the mask (fmha_run :963-966,
+         * fmha_f32 :822-823); read in its own type */
+        if (p->bias)
+            s += ld_in(p->bias, p->elem, b * p->bb + h * p->bh + (int64_t)i * p->br + j);
         if (p->causal && j > i + p->diag) s = -INFINITY;
         work[j] = s;
         if (s > mx) mx = s;

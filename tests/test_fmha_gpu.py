@@ -2,10 +2,11 @@
 (zlift_flash_fwd / zlift_fmha_fwd in libcublas.so.13), against the oracle's
 restatement of the reference attention math (fmha_f32 / fmha_run).
 
-Tolerances: O normwise (max|x - ref| / max|ref|) <= 1e-2; LSE absolute
-<= 1e-3 (LSE is about log(S) ~ 8, so this is ~1e-4 relative).  The
-reference never produces LSE, so the LSE checks pin it against the
-restatement only.
+Tolerances: O normwise (max|x - ref| / max|ref|) <= 1e-2 for 16-bit inputs
+and <= 2e-5 for fp32 inputs (the reference's fmha_f32 path, elem 2); LSE
+absolute <= 1e-3 (LSE is about log(S) ~ 8, so this is ~1e-4 relative;
+<= 1e-5 for fp32).  The reference never produces LSE, so the LSE checks pin
+it against the restatement only.
 """
 import math
 
@@ -32,22 +33,26 @@ def _dev4(a, kind):
     return to_dev(a, kind).view(*a.shape)
 
 
-def run_flash(oracle, kind, B, Sq, Sk, H, Hk, D, causal, seed=1, api="flash"):
+def run_flash(oracle, kind, B, Sq, Sk, H, Hk, D, causal, seed=1, api="flash", bias=False):
     import torch
     import zlift_b200
-    from zlift_b200 import blas
+    from zlift_b200 import blas, inputs
     q, k, v = _qkv(kind, B, Sq, Sk, H, Hk, D, seed)
     scale = 1.0 / math.sqrt(D)
-    elem = 1 if kind == "bf16" else 0
-    o_ref, lse_ref = oracle.attention(q, k, v, causal, scale, elem, kv_ratio=H // Hk)
+    elem = {"bf16": 1, "f16": 0, "f32": 2}[kind]
+    bh = None
+    if bias:
+        bh = inputs.make(kind, "normal", seed + 9, B * H * Sq * Sk).reshape(B, H, Sq, Sk)
+    o_ref, lse_ref = oracle.attention(q, k, v, causal, scale, elem, kv_ratio=H // Hk, bias=bh)
     dq, dk, dv = _dev4(q, kind), _dev4(k, kind), _dev4(v, kind)
     do = torch.full_like(dq, float("nan"))
     dl = torch.full((B, H, Sq), float("nan"), dtype=torch.float32, device=dq.device)
     if api == "flash":
         rc = zlift_b200.flash_forward(dq, dk, dv, do, dl, causal=causal, scale=scale)
     else:
+        db = _dev4(bh, kind) if bias else None
         rc = zlift_b200.fmha_forward(dq, dk, dv, do, dl, mask_type=2 if causal else 0,
-                                     scale=scale)
+                                     scale=scale, bias=db)
     assert rc == 0, f"entry returned {rc}"
     torch.cuda.synchronize()
     assert blas.device_error() == 0
@@ -55,12 +60,13 @@ def run_flash(oracle, kind, B, Sq, Sk, H, Hk, D, causal, seed=1, api="flash"):
     got, want = as_float(o, kind), as_float(o_ref, kind)
     assert np.all(np.isfinite(got))
     err = normwise(got, want)
-    assert err <= O_TOL, f"O normwise error {err:.3e}"
+    o_tol, lse_tol = (2e-5, 1e-5) if kind == "f32" else (O_TOL, LSE_TOL)
+    assert err <= o_tol, f"O normwise error {err:.3e}"
     lse = dl.cpu().numpy()
     fin = np.isfinite(lse_ref)
     np.testing.assert_array_equal(np.isfinite(lse), fin)
     if fin.any():
-        assert np.max(np.abs(lse[fin] - lse_ref[fin])) <= LSE_TOL
+        assert np.max(np.abs(lse[fin] - lse_ref[fin])) <= lse_tol
     return err
 
 
@@ -129,3 +135,47 @@ def test_flash_full_size_sampled(oracle_lib, cuda):
     assert normwise(got, o_ref) <= O_TOL
     lg = lse.cpu().numpy()[bs, hs, is_]
     assert np.max(np.abs(lg - l_ref)) <= LSE_TOL
+
+
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("B,Sq,Sk,H,Hk,D", [(1, 128, 128, 1, 1, 128), (2, 200, 200, 2, 2, 64),
+                                            (1, 96, 300, 4, 2, 128), (1, 300, 130, 2, 1, 40),
+                                            (1, 64, 64, 1, 1, 256)])
+def test_flash_fp32(oracle_lib, cuda, causal, B, Sq, Sk, H, Hk, D):
+    """fp32 inputs (elem 2, the reference's fmha_f32 path, zblas_gpu.cpp:793-844
+    and :1367-1372): GQA, bottom-right causal, odd head dims."""
+    run_flash(oracle_lib, "f32", B, Sq, Sk, H, Hk, D, causal, seed=Sq + D)
+
+
+@pytest.mark.parametrize("kind", ["bf16", "f16", "f32"])
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("Sq,Sk", [(256, 256), (200, 330)])
+def test_fmha_bias(oracle_lib, cuda, kind, causal, Sq, Sk):
+    """xformers block with attn_bias (zblas_gpu.cpp:963-966): the bias, of the
+    input type, is added to the scaled scores before the mask."""
+    run_flash(oracle_lib, kind, 2, Sq, Sk, 2, 2, 128 if kind != "f32" else 64, causal,
+              seed=Sq + Sk, api="fmha", bias=True)
+
+
+def test_fmha_bias_strided(oracle_lib, cuda):
+    """A bias with padded rows (row stride > Sk) and heads broadcast over the
+    batch: strides are honoured, rows need not be 16-byte aligned."""
+    import torch
+    import zlift_b200
+    from zlift_b200 import blas, inputs
+    B, S, H, D = 2, 256, 2, 128
+    q, k, v = _qkv("bf16", B, S, S, H, H, D, 77)
+    full = inputs.make("bf16", "normal", 78, H * S * (S + 3)).reshape(1, H, S, S + 3)
+    bias_h = np.ascontiguousarray(np.broadcast_to(full[:, :, :, :S], (B, H, S, S)))
+    o_ref, lse_ref = oracle_lib.attention(q, k, v, True, 1 / math.sqrt(D), 1, bias=bias_h)
+    dfull = to_dev(full, "bf16").view(1, H, S, S + 3)
+    dbias = dfull[:, :, :, :S].expand(B, H, S, S)      # batch stride 0, row stride S + 3
+    dq, dk, dv = _dev4(q, "bf16"), _dev4(k, "bf16"), _dev4(v, "bf16")
+    do = torch.empty_like(dq)
+    dl = torch.empty(B, H, S, dtype=torch.float32, device=cuda)
+    assert zlift_b200.fmha_forward(dq, dk, dv, do, dl, mask_type=2, bias=dbias) == 0
+    torch.cuda.synchronize()
+    assert blas.device_error() == 0
+    got = as_float(from_dev(do.reshape(-1), "bf16").reshape(q.shape), "bf16")
+    assert normwise(got, as_float(o_ref, "bf16")) <= O_TOL
+    assert np.max(np.abs(dl.cpu().numpy() - lse_ref)) <= LSE_TOL

@@ -121,9 +121,10 @@ def flash_forward(q, k, v, o, lse=None, causal=False, scale=None, stream=None) -
     return load().zlift_flash_fwd(ctypes.byref(blk), ctypes.sizeof(blk), _elem(q), s)
 
 
-def fmha_block(q, k, v, o, lse=None, mask_type=0, scale=None) -> FmhaParams:
+def fmha_block(q, k, v, o, lse=None, mask_type=0, scale=None, bias=None) -> FmhaParams:
     """xformers block for q [B, M, H, K], k/v [B, N, H, K], o [B, M, H, K]
-    contiguous (o row stride H*K)."""
+    contiguous (o row stride H*K); `bias` [B, H, M, N] of q's type (any
+    strides, keys contiguous) is added to the scaled scores."""
     B, M, H, D = q.shape
     N = k.shape[1]
     p = FmhaParams()
@@ -139,10 +140,14 @@ def fmha_block(q, k, v, o, lse=None, mask_type=0, scale=None) -> FmhaParams:
     p.q_strideH, p.k_strideH, p.v_strideH = q.stride(2), k.stride(2), v.stride(2)
     p.q_strideB, p.k_strideB, p.v_strideB = q.stride(0), k.stride(0), v.stride(0)
     p.num_batches, p.num_heads = B, H
+    if bias is not None:
+        p.attn_bias_ptr = bias.data_ptr()
+        p.bias_strideB, p.bias_strideH, p.bias_strideM = (bias.stride(0), bias.stride(1),
+                                                          bias.stride(2))
     return p
 
 
-def fmha_forward(q, k, v, o, lse=None, mask_type=0, scale=None, stream=None) -> int:
-    p = fmha_block(q, k, v, o, lse, mask_type, scale)
+def fmha_forward(q, k, v, o, lse=None, mask_type=0, scale=None, stream=None, bias=None) -> int:
+    p = fmha_block(q, k, v, o, lse, mask_type, scale, bias)
     s = 0 if stream is None else int(getattr(stream, "cuda_stream", stream))
     return load().zlift_fmha_fwd(ctypes.byref(p), ctypes.sizeof(p), _elem(q), s)

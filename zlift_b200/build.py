@@ -34,12 +34,13 @@ NVCC_FLAGS = ARCH + [
     "-I", os.path.join(ROOT, "include"),
 ]
 # kernels whose arithmetic must not be relaxed by --use_fast_math
-PRECISE = {"gemm_simt.cu", "gemm_tc.cu", "cublas_api.cu"}
+PRECISE = {"gemm_simt.cu", "gemm_tc.cu", "cublas_api.cu", "attn_f32.cu"}
 
 SOURCES = [
     "gemm_tc.cu",
     "gemm_simt.cu",
     "fmha.cu",
+    "attn_f32.cu",
     "attention_api.cu",
     "cublas_api.cu",
     "partition.cu",

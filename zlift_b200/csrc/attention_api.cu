@@ -3,13 +3,15 @@
 // internal AttnDesc and the fused forward kernel in fmha.cu.
 //
 // The validation follows the reference's checks line by line (same
-// declines, same meaning of every field), with three differences:
+// declines, same meaning of every field), with these differences:
 //   - an LSE pointer is honoured instead of ignored (flash) or declined
 //     (xformers);
-//   - fp32 inputs are declined (the reference's fp32 path materialises the
-//     full score matrix, fmha_f32 zblas_gpu.cpp:793-844);
-//   - the kernel's own layout limits (head_dim 64 or 128, 16-byte aligned
-//     rows) replace the reference's tile limits (attn_tiles :1398-1423).
+//   - fp32 inputs (elem 2) run on attn_f32.cu's flash-style CUDA-core kernel,
+//     which needs no score scratch, so the reference's 16M-score limit
+//     (attn_tiles, zblas_gpu.cpp:1399-1406) does not apply;
+//   - the kernels' own layout limits (tensor cores: head_dim 64 or 128,
+//     16-byte aligned rows; fp32: head_dim up to 256) replace the reference's
+//     tile limits (attn_tiles :1398-1423).
 #include "fmha.h"
 #include "gemm.h"
 
@@ -56,8 +58,9 @@ int run(const char* who, const zl::AttnDesc& d, cudaStream_t s) {
         return 2;
     }
     if (zl::tracing())
-        fprintf(stderr, "[zblas] %s %s %dx%d heads %d keys %d dim %d\n", who,
-                d.elem == 1 ? "bf16" : "f16", d.batches, d.sq, d.heads, d.sk, d.d);
+        fprintf(stderr, "[zblas] %s %s %dx%d heads %d keys %d dim %d%s\n", who,
+                d.elem == 2 ? "f32" : d.elem == 1 ? "bf16" : "f16", d.batches, d.sq, d.heads,
+                d.sk, d.d, d.bias ? " bias" : "");
     return 0;
 }
 
@@ -94,7 +97,7 @@ int flash_entry(const void* params, unsigned bytes, int elem, cudaStream_t s,
     if (p.b <= 0 || p.h <= 0 || p.seqlen_q <= 0 || p.seqlen_k <= 0) return declined(who, "empty");
     if (p.h_k <= 0 || p.h_h_k_ratio <= 0 || p.h != p.h_k * p.h_h_k_ratio)
         return declined(who, "head grouping");
-    if (elem != 0 && elem != 1) return declined(who, "fp32 inputs");
+    if (elem < 0 || elem > 2) return declined(who, "element type");
     zl::AttnDesc d{};
     d.q = p.q_ptr; d.k = p.k_ptr; d.v = p.v_ptr; d.o = p.o_ptr;
     d.lse = static_cast<float*>(p.softmax_lse_ptr);
@@ -136,8 +139,7 @@ int fmha(const void* params, unsigned bytes, int elem, cudaStream_t s) {
     if (p.num_batches <= 0 || p.num_heads <= 0 || p.num_queries <= 0 || p.num_keys <= 0)
         return declined(who, "empty");
     if (p.head_dim != p.head_dim_value) return declined(who, "head_dim != head_dim_value");
-    if (p.attn_bias_ptr) return declined(who, "attention bias");
-    if (elem != 0 && elem != 1) return declined(who, "fp32 inputs");
+    if (elem < 0 || elem > 2) return declined(who, "element type");
     zl::AttnDesc d{};
     d.q = p.query_ptr; d.k = p.key_ptr; d.v = p.value_ptr; d.o = p.output_ptr;
     d.lse = static_cast<float*>(p.logsumexp_ptr);
@@ -148,6 +150,10 @@ int fmha(const void* params, unsigned bytes, int elem, cudaStream_t s) {
     d.ob = (long long)p.num_queries * p.o_strideM;
     d.oh = p.head_dim_value;
     d.orr = p.o_strideM;
+    // additive bias [b*strideB + h*strideH + query*strideM + key] of the input
+    // type, added after scaling (zblas_gpu.cpp:963-966, :1451-1452)
+    d.bias = p.attn_bias_ptr;
+    d.bb = p.bias_strideB; d.bh = p.bias_strideH; d.br = p.bias_strideM;
     d.batches = p.num_batches; d.heads = p.num_heads; d.kv_ratio = 1;
     d.sq = p.num_queries; d.sk = p.num_keys; d.d = p.head_dim;
     d.scale = p.scale;

@@ -72,33 +72,15 @@ struct FParams {
     float scale, scale_log2;
     int causal, diag;
     int half_p;                  // P.V starts on the first half of P (see the MMA issuer)
+    const uint16_t* bias;        // BIAS kernels: [b*bb + h*bh + query*br + key]
+    long long bb, bh, br;
+    int bias_vec;                // rows start 16-byte aligned: vector loads
 };
 
 __device__ __forceinline__ float ex2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
-}
-
-// 2^x on the FMA/ALU pipes, for a share of the softmax exponentials so that
-// the MUFU unit (16 exp2 per clock per SM, as busy as the tensor core at
-// head_dim 128) is not the bottleneck.  Cody-Waite range reduction:
-// x = j + f with j = round(x) (obtained by adding 1.5 * 2^23, which leaves j
-// in the low mantissa bits) and f in [-1/2, 1/2]; 2^f from a degree-3
-// polynomial of least maximum relative error (Remez exchange, 7.5e-5; see
-// fit_exp2_poly.py); 2^j applied by adding j to the exponent field.
-// Arguments below -126 (masked scores are -inf) give exactly 0.
-__device__ __forceinline__ float ex2_poly(float x) {
-    constexpr float kC0 = 0.9999280571937561f, kC1 = 0.6932609677314758f,
-                    kC2 = 0.2426111251115799f, kC3 = 0.0551716685295105f;
-    constexpr float kShift = 12582912.0f;       // 1.5 * 2^23
-    const float xc = fmaxf(x, -126.0f);
-    const float t = xc + kShift;
-    const float f = xc - (t - kShift);
-    const int j = __float_as_int(t) - 0x4B400000;
-    const float p = fmaf(fmaf(fmaf(kC3, f, kC2), f, kC1), f, kC0);
-    const float y = __int_as_float(__float_as_int(p) + (j << 23));
-    return x < -126.0f ? 0.0f : y;
 }
 
 template <bool BF16>
@@ -122,9 +104,41 @@ __device__ __forceinline__ int key_tiles(const FParams& p, int q0) {
     return min(last_key / BKEY + 1, p.nkt);
 }
 
-// POLY: 0 = every exponential on MUFU; k > 0 = one column pair in k by
-// ex2_poly on the FMA pipe.
-template <int D, bool BF16, int POLY>
+// Adds an additive bias row (16-bit, this thread's query row, keys
+// key0..key0+127) to the raw scores in log2 units: s = s * c + bias * log2(e).
+// Keys at or past `nvalid` get no bias (the mask sets them to -inf).
+template <bool BF16>
+__device__ __forceinline__ void bias_row(float (&s)[BKEY], const uint16_t* row, int nvalid,
+                                         float c, bool vec) {
+    constexpr float kLog2e = 1.4426950408889634f;
+    auto cvt = [](uint32_t h) {
+        if constexpr (BF16) return __uint_as_float(h << 16);
+        else return __half2float(__ushort_as_half((unsigned short)h));
+    };
+    if (vec && nvalid >= BKEY) {
+#pragma unroll
+        for (int g = 0; g < BKEY / 8; g++) {
+            const uint4 w = __ldg(reinterpret_cast<const uint4*>(row) + g);
+            const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int t = 0; t < 4; t++) {
+                s[8 * g + 2 * t] = fmaf(s[8 * g + 2 * t], c, cvt(u[t] & 0xffffu) * kLog2e);
+                s[8 * g + 2 * t + 1] = fmaf(s[8 * g + 2 * t + 1], c, cvt(u[t] >> 16) * kLog2e);
+            }
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < BKEY; i++) {
+            const float bv = i < nvalid ? cvt(__ldg(row + i)) : 0.f;
+            s[i] = fmaf(s[i], c, bv * kLog2e);
+        }
+    }
+}
+
+// BIAS: an additive bias of the input type is read from global memory for
+// every score (the xformers block's attn_bias, zblas/zblas_gpu.cpp:963-966);
+// scores are then kept in log2 units with the bias added before the mask.
+template <int D, bool BF16, bool BIAS>
 __global__ void __launch_bounds__(kThreads, 1)
 fmha_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
                 const __grid_constant__ CUtensorMap tmK,
@@ -327,7 +341,13 @@ fmha_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
         const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
         const uint32_t s_addr = tmem_base + lane_off + (t ? C::S_COL1 : C::S_COL0);
         const uint32_t o_addr = tmem_base + lane_off + (t ? C::O_COL1 : C::O_COL0);
-        const float c = p.scale_log2;
+        // with a bias the scores are turned into log2 units (biased) right
+        // after the load, and the rest of the softmax works with c = 1
+        const float c = BIAS ? 1.f : p.scale_log2;
+        const uint16_t* brow = nullptr;
+        if constexpr (BIAS)
+            brow = p.bias + (long long)b * p.bb + (long long)h * p.bh +
+                   (long long)min(qrow, p.sq - 1) * p.br;
         float m_used = -INFINITY, l = 0.f;
         bool alive = true;
         for (int j = 0; j < tnt; j++) {
@@ -339,6 +359,7 @@ fmha_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
                 tmem_ld32(s_addr + c0, *reinterpret_cast<uint32_t(*)[32]>(&s[c0]));
             tmem_wait_ld();
             const int key0 = j * BKEY;
+            if constexpr (BIAS) bias_row<BF16>(s, brow + key0, p.sk - key0, p.scale_log2, p.bias_vec);
             const bool edge = (key0 + BKEY > p.sk) || (p.causal && key0 + BKEY - 1 > tq0 + p.diag);
             if (edge) {
                 const int lim = p.causal ? min(p.sk - 1, qrow + p.diag) : p.sk - 1;
@@ -379,8 +400,7 @@ fmha_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
                 }
             }
             const float mc = m_used == -INFINITY ? 0.f : m_used * c;
-            // exponentials: one column pair in POLY on the FMA pipe
-            // (ex2_poly), the rest on MUFU; row sum over 8 partial sums
+            // exponentials on MUFU; row sum over 8 partial sums
             float sum8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
             uint32_t pk[BKEY / 2];
             // two halves of the keys: P of keys 0-63 is stored and announced
@@ -391,14 +411,7 @@ fmha_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
 #pragma unroll
                 for (int i = half * (BKEY / 4); i < (half + 1) * (BKEY / 4); i++) {
                     const float x0 = fmaf(s[2 * i], c, -mc), x1 = fmaf(s[2 * i + 1], c, -mc);
-                    float p0, p1;
-                    if (POLY > 0 && i % (POLY > 0 ? POLY : 1) == (POLY > 0 ? POLY : 1) - 1) {
-                        p0 = ex2_poly(x0);
-                        p1 = ex2_poly(x1);
-                    } else {
-                        p0 = ex2(x0);
-                        p1 = ex2(x1);
-                    }
+                    const float p0 = ex2(x0), p1 = ex2(x1);
                     sum8[i & 7] += p0 + p1;
                     pk[i] = pack2<BF16>(p0, p1);
                 }
@@ -447,7 +460,9 @@ fmha_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
             }
         }
         if (row_ok && p.lse) {
-            const float lse = l > 0.f ? m_used * p.scale + logf(l) : -INFINITY;
+            // (m_used is in raw-score units, or in log2 units with a bias)
+            const float lse_scale = BIAS ? 0.6931471805599453f : p.scale;
+            const float lse = l > 0.f ? m_used * lse_scale + logf(l) : -INFINITY;
             p.lse[bh * (long long)p.sq + qrow] = lse;
         }
     }
@@ -496,11 +511,11 @@ bool attn_tmap(CUtensorMap* tm, int elem, const void* base, int d, int seq, int 
     return r == CUDA_SUCCESS;
 }
 
-template <int D, bool BF16, int POLY>
-int launch_poly(const AttnDesc& d, const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v,
-           const FParams& p, long long grid, cudaStream_t s) {
+template <int D, bool BF16, bool BIAS>
+int launch(const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v, const FParams& p,
+           long long grid, cudaStream_t s) {
     using C = FCfg<D>;
-    auto kern = fmha_fwd_kernel<D, BF16, POLY>;
+    auto kern = fmha_fwd_kernel<D, BF16, BIAS>;
     static std::atomic<unsigned long long> attr_set{0};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -516,26 +531,11 @@ int launch_poly(const AttnDesc& d, const CUtensorMap& q, const CUtensorMap& k, c
     return e == cudaSuccess ? 0 : (int)e;
 }
 
-// Share of the exponentials computed by polynomial: ZBLAS_FMHA_POLY = 0 (all
-// on MUFU), 4 or 8 (one column pair in 4 or 8); default 0.
-int poly_share() {
-    static int v = -1;
-    if (v < 0) {
-        const char* e = getenv("ZBLAS_FMHA_POLY");
-        const int x = e ? atoi(e) : 0;
-        v = (x == 4 || x == 8) ? x : 0;
-    }
-    return v;
-}
-
 template <int D, bool BF16>
-int launch(const AttnDesc& d, const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v,
-           const FParams& p, long long grid, cudaStream_t s) {
-    switch (poly_share()) {
-    case 4: return launch_poly<D, BF16, 4>(d, q, k, v, p, grid, s);
-    case 8: return launch_poly<D, BF16, 8>(d, q, k, v, p, grid, s);
-    default: return launch_poly<D, BF16, 0>(d, q, k, v, p, grid, s);
-    }
+int launch_bias(const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v,
+                const FParams& p, long long grid, cudaStream_t s) {
+    return p.bias ? launch<D, BF16, true>(q, k, v, p, grid, s)
+                  : launch<D, BF16, false>(q, k, v, p, grid, s);
 }
 
 bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -543,6 +543,7 @@ bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 }  // namespace
 
 int fmha_fwd(const AttnDesc& d, cudaStream_t s) {
+    if (d.elem == 2) return attn_f32_fwd(d, s);
     if (d.elem != 0 && d.elem != 1) return 1;
     if (d.d != 64 && d.d != 128) return 1;
     if (d.batches <= 0 || d.heads <= 0 || d.sq <= 0 || d.sk <= 0 || d.kv_ratio <= 0) return 1;
@@ -579,13 +580,17 @@ int fmha_fwd(const AttnDesc& d, cudaStream_t s) {
     // P.V on all of P at once (one wait per tile and key tile) measured 2-6 %
     // faster than starting on its first half; ZBLAS_FMHA_HALF=1 restores that
     p.half_p = getenv("ZBLAS_FMHA_HALF") ? 1 : 0;
+    p.bias = static_cast<const uint16_t*>(d.bias);
+    p.bb = d.bb; p.bh = d.bh; p.br = d.br;
+    p.bias_vec = d.bias && al16(d.bias) && (d.br * 2) % 16 == 0 && (d.bh * 2) % 16 == 0 &&
+                 (d.bb * 2) % 16 == 0;
     const long long grid = (long long)p.npairs * p.bh_count;
     if (grid > 0x7fffffffLL) return 1;
     if (d.d == 128)
-        return d.elem == 1 ? launch<128, true>(d, tq, tk, tv, p, grid, s)
-                           : launch<128, false>(d, tq, tk, tv, p, grid, s);
-    return d.elem == 1 ? launch<64, true>(d, tq, tk, tv, p, grid, s)
-                       : launch<64, false>(d, tq, tk, tv, p, grid, s);
+        return d.elem == 1 ? launch_bias<128, true>(tq, tk, tv, p, grid, s)
+                           : launch_bias<128, false>(tq, tk, tv, p, grid, s);
+    return d.elem == 1 ? launch_bias<64, true>(tq, tk, tv, p, grid, s)
+                       : launch_bias<64, false>(tq, tk, tv, p, grid, s);
 }
 
 int fmha_set_wait_limit(unsigned long long ns) { return set_unit_wait_limit(ns); }

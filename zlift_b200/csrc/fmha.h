@@ -19,7 +19,12 @@ struct AttnDesc {
     float scale;                  // applied to Q.K^T, natural-log units
     bool causal;
     int diag;                     // key j is masked for query i when j > i + diag
-    int elem;                     // 0 fp16, 1 bf16
+    int elem;                     // 0 fp16, 1 bf16, 2 fp32
+    // Optional additive bias of the input type, added to the scaled scores
+    // before the causal mask (zblas/zblas_gpu.cpp:963-966, :822-823):
+    // bias[b*bb + h*bh + query*br + key], strides in elements.  Null: none.
+    const void* bias;
+    long long bb, bh, br;
     // Optional sub-range of (batch, head) pairs, for the partition layer:
     // the kernel covers pairs [pair_begin, pair_end) of batches*heads in
     // batch-major order.  pair_end == 0 means all.
@@ -29,6 +34,9 @@ struct AttnDesc {
 // 0 = enqueued, 1 = declined (shape/layout outside this kernel), > 1 = CUDA
 // error code of the launch.
 int fmha_fwd(const AttnDesc& d, cudaStream_t s);
+
+// fp32 attention on the CUDA cores (elem == 2), same return convention.
+int attn_f32_fwd(const AttnDesc& d, cudaStream_t s);
 
 // Decodes a FlashAttention-2 parameter block and runs it (attention_api.cu);
 // pair_end > 0 restricts it to (batch, head) pairs [pair_begin, pair_end).

@@ -810,41 +810,69 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                     if (lane == 0) release_acc(&tempty[acc], rank);
                     continue;
                 }
+                if (!use_beta) {
+                    // C is not read: one barrier per chunk, and the TMEM load
+                    // of chunk c+1 in flight while chunk c is converted.  The
+                    // leader waits for the store of chunk c-1 to have read its
+                    // buffer before the barrier, which then frees that buffer
+                    // for chunk c+1; no wait inside can fail, so the barrier
+                    // needs no vote.
+                    uint32_t v[32], vn[32];
+                    tmem_ld32(taddr, v);
+                    tmem_wait_ld();
+#pragma unroll 1
+                    for (int c0 = 0; c0 < ncols; c0 += kEpiCols, chunk++) {
+                        uint8_t* sbuf = epi + (chunk & 1) * C_::EPI_BUF;
+                        const bool more = c0 + kEpiCols < ncols;
+                        if (more) tmem_ld32(taddr + c0 + kEpiCols, vn);
+                        convert_chunk<OUT>(v, sbuf, r_in_tile, alpha, beta, ia, ib, false, p.epi,
+                                           bias_row);
+                        fence_async_smem();
+                        if (leader) bulk_wait_read<0>();
+                        named_bar_sync(1, 128);
+                        if (leader) {
+                            tma_store_3d(&tmC, sbuf, m0, n0 + c0, b);
+                            bulk_commit();
+                        }
+                        if (more) {
+                            tmem_wait_ld();
+#pragma unroll
+                            for (int j = 0; j < 32; j++) v[j] = vn[j];
+                        }
+                    }
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) release_acc(&tempty[acc], rank);
+                    continue;
+                }
 #pragma unroll 1
                 for (int c0 = 0; c0 < ncols; c0 += kEpiCols, chunk++) {
                     const int buf = chunk & 1;
                     uint8_t* sbuf = epi + buf * C_::EPI_BUF;
                     if (leader) {
-                        if (use_beta) {
-                            // C chunks are loaded one chunk ahead: a tile's first
-                            // chunk here, chunk c+1 into the other buffer once the
-                            // store that last used it has read it
-                            if (c0 == 0) {
-                                bulk_wait_read<1>();   // store of chunk-2 has read sbuf
-                                mbar_expect_tx(&cbar[buf], C_::EPI_BUF);
-                                tma_load_3d(sbuf, &tmC, &cbar[buf], m0, n0 + c0, b);
-                            }
-                            if (c0 + kEpiCols < ncols) {
-                                bulk_wait_read<0>();   // store of chunk-1 has read the other buffer
-                                mbar_expect_tx(&cbar[buf ^ 1], C_::EPI_BUF);
-                                tma_load_3d(epi + (buf ^ 1) * C_::EPI_BUF, &tmC, &cbar[buf ^ 1], m0,
-                                            n0 + c0 + kEpiCols, b);
-                            }
-                        } else {
-                            bulk_wait_read<1>();       // store of chunk-2 has read sbuf
+                        // C chunks are loaded one chunk ahead: a tile's first
+                        // chunk here, chunk c+1 into the other buffer once the
+                        // store that last used it has read it
+                        if (c0 == 0) {
+                            bulk_wait_read<1>();   // store of chunk-2 has read sbuf
+                            mbar_expect_tx(&cbar[buf], C_::EPI_BUF);
+                            tma_load_3d(sbuf, &tmC, &cbar[buf], m0, n0 + c0, b);
+                        }
+                        if (c0 + kEpiCols < ncols) {
+                            bulk_wait_read<0>();   // store of chunk-1 has read the other buffer
+                            mbar_expect_tx(&cbar[buf ^ 1], C_::EPI_BUF);
+                            tma_load_3d(epi + (buf ^ 1) * C_::EPI_BUF, &tmC, &cbar[buf ^ 1], m0,
+                                        n0 + c0 + kEpiCols, b);
                         }
                     }
                     uint32_t v[32];
                     tmem_ld32(taddr + c0, v);
-                    bool w = true;
-                    if (use_beta) {
-                        w = mbar_wait(&cbar[buf], (cphase >> buf) & 1u, abort_flag);
-                        cphase ^= 1u << buf;
-                    }
+                    bool w = mbar_wait(&cbar[buf], (cphase >> buf) & 1u, abort_flag);
+                    cphase ^= 1u << buf;
                     tmem_wait_ld();
                     ok = named_bar_and(1, 128, w);
                     if (!ok) break;
-                    convert_chunk<OUT>(v, sbuf, r_in_tile, alpha, beta, ia, ib, use_beta, p.epi,
+                    convert_chunk<OUT>(v, sbuf, r_in_tile, alpha, beta, ia, ib, true, p.epi,
                                        bias_row);
                     fence_async_smem();
                     named_bar_sync(1, 128);
