@@ -91,6 +91,15 @@ ZLIFT_API cublasStatus_t cublasSgemm_v2(cublasHandle_t handle, int transa, int t
                               const float *A, int lda, const float *B, int ldb,
                               const float *beta, float *C, int ldc);
 
+/* fp64 GEMM.  zblas/zblas.c:131-144 (cublasDgemm_v2: oneMKL on the GPU,
+ * zblas_gpu.cpp:1548-1559, else cblas_dgemm on the host).  Here: a CUDA-core
+ * fp64 kernel (B200's tensor cores have no fp64 form in tcgen05); alpha and
+ * beta are double, host or device pointer mode. */
+ZLIFT_API cublasStatus_t cublasDgemm_v2(cublasHandle_t handle, int transa, int transb, int m,
+                                        int n, int k, const double *alpha, const double *A,
+                                        int lda, const double *B, int ldb, const double *beta,
+                                        double *C, int ldc);
+
 /* Mixed-type GEMM.  Replaces zblas/zblas.c:357-391.
  *   A,B fp16  -> C fp16 or fp32, compute 32F (0 or 68)
  *   A,B bf16  -> C bf16 or fp32, compute 32F

@@ -66,6 +66,9 @@ def oracle() -> ctypes.CDLL:
         lib.zo_gemm_entries.restype = None
         lib.zo_gemm_entries.argtypes = [_int, _int, _int, _d, _vp, _int, _int, _vp, _int,
                                         _int, _d, _vp, _int, _int, _vp, _vp, _ll, _vp]
+        lib.zo_dgemm.restype = None
+        lib.zo_dgemm.argtypes = [_int, _int, _int, _int, _int, _d, _vp, _int, _vp, _int, _d,
+                                 _vp, _int]
         lib.zo_lt_epilogue.restype = None
         lib.zo_lt_epilogue.argtypes = [_vp, _int, _int, _int, _int, _ll, _int, _vp, _int]
         lib.zo_attention.restype = _int
@@ -128,6 +131,12 @@ def gemm_strided_batched_ex(transa, transb, m, n, k, alpha, A, Atype, lda, sA, B
     return oracle().zo_gemm_strided_batched_ex(transa, transb, m, n, k, _p(al), _p(A), Atype,
                                                lda, sA, _p(B), Btype, ldb, sB, _p(be), _p(C),
                                                Ctype, ldc, sC, batch, compute)
+
+
+def dgemm(transa, transb, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc) -> None:
+    """Oracle restatement of cublasDgemm_v2 on host float64 arrays (C in place)."""
+    oracle().zo_dgemm(transa, transb, m, n, k, float(alpha), _p(A), lda, _p(B), ldb,
+                      float(beta), _p(C), ldc)
 
 
 def lt_epilogue(D, Dtype, m, n, ldd, strideD, batch, bias, flags) -> None:

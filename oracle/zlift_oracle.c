@@ -22,6 +22,8 @@
  *       CUDA_R_32I, compute 32I) has no counterpart in the reference (which
  *       returns NOT_SUPPORTED, zblas/zblas.c:366-367); it is exact int32
  *       arithmetic with two's-complement wrap for alpha/beta scaling.
+ *   zo_dgemm                              cblas_dgemm as called at
+ *       zblas/zblas.c:131-144 (fp64, summed in K order).
  *   zo_gemm_strided_batched_ex            zblas/zblas.c:491-511 (host loop
  *       over the batch; strides in elements, elem_size :488-490).
  *   zo_lt_epilogue                        cublasLtMatmul's bias / ReLU /
@@ -188,6 +190,24 @@ static int8_t *pack_i8(int op, const int8_t *X, int rows, int k, int ld, int is_
             /* A: op(A)(r, l); B: op(B)(l, r) */
             p[(size_t)r * k + l] = is_b ? X[opidx(op, l, r, ld)] : X[opidx(op, r, l, ld)];
     return p;
+}
+
+/* fp64 GEMM restating cblas_dgemm (zblas/zblas.c:131-144): products summed
+ * in fp64 in K order, C = alpha*sum + beta*C (beta == 0 does not read C). */
+void zo_dgemm(int transa, int transb, int m, int n, int k, double alpha,
+              const double *A, int lda, const double *B, int ldb, double beta,
+              double *C, int ldc) {
+#pragma omp parallel for schedule(static)
+    for (int j = 0; j < n; j++) {
+        for (int i = 0; i < m; i++) {
+            double acc = 0.0;
+            for (int l = 0; l < k; l++)
+                acc += A[opidx(transa, i, l, lda)] * B[opidx(transb, l, j, ldb)];
+            double c = alpha * acc;
+            if (beta != 0.0) c += beta * C[i + (int64_t)j * ldc];
+            C[i + (int64_t)j * ldc] = c;
+        }
+    }
 }
 
 /* int8 x int8 -> int32 with int32 alpha/beta; exact, wrapping.  Both

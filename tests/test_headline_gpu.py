@@ -243,3 +243,82 @@ def test_nsplit_overlap_one_rank_equals_one_shot(handle):
     torch.cuda.synchronize()
     assert blas.device_error() == 0
     assert torch.equal(one, got)
+
+
+@pytest.mark.parametrize("ta,tb,m,n,k,alpha,beta", [
+    (0, 0, 256, 192, 320, 1.0, 0.0),
+    (1, 1, 100, 70, 131, -0.5, 2.0),
+    (0, 1, 65, 257, 64, 2.0, 1.0),
+])
+def test_dgemm(handle, oracle_lib, ta, tb, m, n, k, alpha, beta):
+    """cublasDgemm_v2 (zblas/zblas.c:131-144) vs the oracle's fp64 GEMM,
+    normwise <= 1e-12 (both sum fp64 products, in different orders)."""
+    import torch
+    from zlift_b200 import blas, inputs
+    ar, ac = (m, k) if ta == 0 else (k, m)
+    br, bc = (k, n) if tb == 0 else (n, k)
+    A = inputs.uniform(51, ar * ac)
+    B = inputs.uniform(52, br * bc)
+    C0 = inputs.uniform(53, m * n)
+    want = C0.copy()
+    oracle_lib.dgemm(ta, tb, m, n, k, alpha, A, ar, B, br, beta, want, m)
+    dA = torch.from_numpy(A).cuda()
+    dB = torch.from_numpy(B).cuda()
+    dC = torch.from_numpy(np.concatenate([C0, np.full(CANARY, 7.0)])).cuda()
+    assert handle.dgemm(ta, tb, m, n, k, alpha, dA, ar, dB, br, beta, dC, m) == 0
+    out = dC.cpu().numpy()
+    assert blas.device_error() == 0
+    assert np.all(out[-CANARY:] == 7.0)
+    assert normwise(out[:-CANARY], want) <= 1e-12
+
+
+def test_fp16_output_edges(handle, oracle_lib):
+    """fp16 outputs in the subnormal, overflow and NaN ranges, against the
+    oracle's converter, which restates the reference's (zblas/zblas.c:
+    260-277: round to nearest even for normals, truncation for subnormals,
+    overflow to inf -- and NaN to inf too, since a NaN's exponent takes the
+    overflow branch).  Deviations, stated here and bounded: the kernels
+    round subnormals to nearest even, so a subnormal output may differ from
+    the reference by one subnormal ulp (2^-24) and by no more; a NaN output
+    stays NaN (IEEE, as NVIDIA's cuBLAS), where the reference writes inf.
+    Overflows give the same infinities."""
+    from zlift_b200 import blas, inputs
+    m = n = 128
+    k = 64
+    A = inputs.make("f16", "uniform", 61, m * k)
+    B = inputs.make("f16", "uniform", 62, k * n)
+    Bf = inputs.bits_to_float(B, "f16").copy()
+    Bf[5 * k + 3] = np.nan                         # column 5 of op(B) has a NaN
+    B = Bf.astype(np.float16).view(np.uint16)
+    for alpha, what in ((2.0 ** -18, "subnormal"), (2.0 ** 14, "overflow")):
+        C0 = np.zeros(m * n, np.uint16)
+        want = C0.copy()
+        assert oracle_lib.gemm_ex(0, 0, m, n, k, alpha, A, 2, m, B, 2, k, 0.0, want, 2, m) == 0
+        dA, dB = to_dev(A, "f16"), to_dev(B, "f16")
+        dC = to_dev(C0, "f16")
+        assert handle.gemm_ex(0, 0, m, n, k, alpha, dA, 2, m, dB, 2, k, 0.0, dC, 2, m) == 0
+        got = from_dev(dC, "f16")
+        assert blas.device_error() == 0
+        g = got.view(np.float16).astype(np.float64)
+        w = want.view(np.float16).astype(np.float64)
+        col5 = np.zeros((n, m), bool)
+        col5[5] = True
+        col5 = col5.reshape(-1)
+        assert np.isnan(g[col5]).all()                     # NaN stays NaN here ...
+        assert np.isinf(w[col5]).all()                     # ... the reference writes inf
+        assert not np.isnan(g[~col5]).any() and not np.isnan(w[~col5]).any()
+        fin = ~col5
+        inf_w = np.isinf(w) & fin
+        np.testing.assert_array_equal(g[inf_w], w[inf_w])  # same infinities
+        rest = fin & ~inf_w
+        sub = rest & (np.abs(w) < 2.0 ** -14)
+        if what == "subnormal":
+            assert sub.sum() > m * n // 2                  # most outputs are subnormal
+            assert np.max(np.abs(g[sub] - w[sub])) <= 2.0 ** -24
+        else:
+            assert inf_w.sum() > 0                         # some outputs overflowed
+        nrm = rest & ~sub
+        if nrm.any():
+            # normal outputs: both round the same fp32 sum to nearest even,
+            # up to the fp32 summation order
+            assert normwise(g[nrm], w[nrm]) <= 1e-2

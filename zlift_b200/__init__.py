@@ -40,6 +40,8 @@ SIGNATURES = [
     ("cublasGetStatusString", ctypes.c_char_p, [c_int]),
     ("cublasSgemm_v2", c_int, [c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p,
                                c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_int]),
+    ("cublasDgemm_v2", c_int, [c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p,
+                               c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_int]),
     ("cublasGemmEx", c_int, [c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p,
                              c_void_p, c_int, c_int, c_void_p, c_int, c_int, c_void_p,
                              c_void_p, c_int, c_int, c_int, c_int]),

@@ -108,6 +108,12 @@ class Handle:
                                        self._scalar(alpha, False), _ptr(A), lda, _ptr(B), ldb,
                                        self._scalar(beta, False), _ptr(C), ldc)
 
+    def dgemm(self, transa, transb, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc) -> int:
+        al, be = ctypes.c_double(float(alpha)), ctypes.c_double(float(beta))
+        return self.lib.cublasDgemm_v2(self.h, transa, transb, m, n, k, ctypes.byref(al),
+                                       _ptr(A), lda, _ptr(B), ldb, ctypes.byref(be), _ptr(C),
+                                       ldc)
+
     def gemm_ex(self, transa, transb, m, n, k, alpha, A, Atype, lda, B, Btype, ldb,
                 beta, C, Ctype, ldc, compute=COMPUTE_32F, algo=0) -> int:
         self._keep.clear()

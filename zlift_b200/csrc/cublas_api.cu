@@ -443,6 +443,23 @@ cublasStatus_t cublasSgemm_v2(cublasHandle_t handle, int transa, int transb, int
                    C, kR32F, ldc, 0, 1, CUBLAS_COMPUTE_32F);
 }
 
+cublasStatus_t cublasDgemm_v2(cublasHandle_t handle, int transa, int transb, int m, int n,
+                              int k, const double* alpha, const double* A, int lda,
+                              const double* B, int ldb, const double* beta, double* C, int ldc) {
+    Handle* h = as_handle(handle);
+    if (!h) return CUBLAS_STATUS_NOT_INITIALIZED;
+    cublasStatus_t st = check_dims(transa, transb, m, n, k, lda, ldb, ldc);
+    if (st) return st;
+    if (m == 0 || n == 0) return CUBLAS_STATUS_SUCCESS;
+    if (!alpha || !beta || !C || (k > 0 && (!A || !B))) return CUBLAS_STATUS_INVALID_VALUE;
+    const bool dev = h->pointer_mode == CUBLAS_POINTER_MODE_DEVICE;
+    trace("dgemm %dx%dx%d ta=%d tb=%d", m, n, k, transa, transb);
+    return map_launch(dgemm_simt(transa == CUBLAS_OP_N ? 0 : 1, transb == CUBLAS_OP_N ? 0 : 1, m,
+                                 n, k, dev ? 0.0 : *alpha, dev ? 0.0 : *beta,
+                                 dev ? alpha : nullptr, dev ? beta : nullptr, A, lda, B, ldb, C,
+                                 ldc, h->stream));
+}
+
 cublasStatus_t cublasGemmEx(cublasHandle_t handle, int transa, int transb, int m, int n, int k,
                             const void* alpha, const void* A, int Atype, int lda,
                             const void* B, int Btype, int ldb, const void* beta, void* C,

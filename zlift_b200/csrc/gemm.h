@@ -94,6 +94,12 @@ int split_tf32(const float* X, bool k_contig, long long MN, long long K, long lo
                long long stride, int batch, long long kp, float* hi, float* lo,
                cudaStream_t s);
 
+// fp64 GEMM on the CUDA cores (column-major, op 0 = N, 1 = T/C); alpha and
+// beta from the host values unless the *_dev pointers are set.
+int dgemm_simt(int transa, int transb, int m, int n, int k, double alpha, double beta,
+               const double* alpha_dev, const double* beta_dev, const double* A, long long lda,
+               const double* B, long long ldb, double* C, long long ldc, cudaStream_t s);
+
 int num_sms();
 
 // Count of kernels this library has launched (all devices, all streams).

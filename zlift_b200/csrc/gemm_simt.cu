@@ -221,6 +221,87 @@ int split_tf32(const float* X, bool k_contig, long long MN, long long K, long lo
     return e == cudaSuccess ? 0 : (int)e;
 }
 
+namespace {
+
+// fp64 GEMM (cublasDgemm_v2; the reference hands it to oneMKL on the GPU,
+// zblas/zblas_gpu.cpp:1548-1559, or cblas_dgemm on the host,
+// zblas/zblas.c:131-144).  64 x 64 output tile per 256 threads, each thread
+// a 4 x 4 block (rows ty*4.., columns tx + 16c), K in slices of 16 through
+// shared memory; fp64 FMA in K order.
+constexpr int DT = 64, DK = 16;
+
+__global__ void __launch_bounds__(256) dgemm_kernel(int transa, int transb, int m, int n, int k,
+                                                    double alpha, double beta,
+                                                    const double* alpha_dev,
+                                                    const double* beta_dev,
+                                                    const double* __restrict__ A, long long lda,
+                                                    const double* __restrict__ B, long long ldb,
+                                                    double* __restrict__ C, long long ldc) {
+    __shared__ double sa[DK][DT + 1];
+    __shared__ double sb[DK][DT + 1];
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+    const int i0 = blockIdx.x * DT, j0 = blockIdx.y * DT;
+    double acc[4][4] = {};
+    for (int l0 = 0; l0 < k; l0 += DK) {
+        for (int e = threadIdx.x; e < DK * DT; e += 256) {
+            // transa == N reads down a column (i fastest): coalesced for N,
+            // strided for T
+            const int r = transa == 0 ? e % DT : e / DK, l = transa == 0 ? e / DT : e % DK;
+            const long long gi = i0 + r, gl = l0 + l;
+            sa[l][r] = (gi < m && gl < k) ? A[opidx(transa, gi, gl, lda)] : 0.0;
+        }
+        for (int e = threadIdx.x; e < DK * DT; e += 256) {
+            const int c = transb == 0 ? e / DK : e % DT, l = transb == 0 ? e % DK : e / DT;
+            const long long gj = j0 + c, gl = l0 + l;
+            sb[l][c] = (gj < n && gl < k) ? B[opidx(transb, gl, gj, ldb)] : 0.0;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int l = 0; l < DK; l++) {
+            double a[4], b[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) a[i] = sa[l][ty * 4 + i];
+#pragma unroll
+            for (int c = 0; c < 4; c++) b[c] = sb[l][tx + 16 * c];
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int c = 0; c < 4; c++) acc[i][c] = fma(a[i], b[c], acc[i][c]);
+        }
+        __syncthreads();
+    }
+    if (alpha_dev) alpha = *alpha_dev;
+    if (beta_dev) beta = *beta_dev;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const long long gi = i0 + ty * 4 + i;
+        if (gi >= m) continue;
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+            const long long gj = j0 + tx + 16 * c;
+            if (gj >= n) continue;
+            double* cp = C + gi + gj * ldc;
+            // beta == 0 does not read C (BLAS convention)
+            *cp = beta != 0.0 ? fma(beta, *cp, alpha * acc[i][c]) : alpha * acc[i][c];
+        }
+    }
+}
+
+}  // namespace
+
+int dgemm_simt(int transa, int transb, int m, int n, int k, double alpha, double beta,
+               const double* alpha_dev, const double* beta_dev, const double* A, long long lda,
+               const double* B, long long ldb, double* C, long long ldc, cudaStream_t s) {
+    if (m <= 0 || n <= 0) return 0;
+    const long long gx = (m + DT - 1) / DT, gy = (n + DT - 1) / DT;
+    if (gx > 0x7fffffffLL || gy > 65535) return 1;
+    dgemm_kernel<<<dim3((unsigned)gx, (unsigned)gy), 256, 0, s>>>(
+        transa, transb, m, n, k, alpha, beta, alpha_dev, beta_dev, A, lda, B, ldb, C, ldc);
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) note_launch();
+    return e == cudaSuccess ? 0 : (int)e;
+}
+
 // A wait that nothing completes: one thread initialises an mbarrier that
 // expects one arrival and waits on its first phase with `limit_ns`.  No
 // copy or MMA is in flight, so the kernel simply returns after the limit,
