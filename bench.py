@@ -17,12 +17,12 @@ those of gemm_f16, the configuration the metric is quoted on, and
                      alpha=1/sqrt(512), beta=0; N>1: batch split across GPUs
                      (zlift_part_gemm_strided_batched_ex), no collective.
   gemm_i8            cublasGemmEx int8 -> int32, M=2048 K=4096 N=14336, TN;
-                     N>1: N-column split with the NCCL all-gather of C
-                     overlapping the GEMM sub-block by sub-block
-                     (zlift_part_gemm_ex_nsplit_overlap); also reported with
-                     the gather after the whole GEMM (gemm_i8_serialgather,
-                     zlift_part_gemm_ex_nsplit) and without it
-                     (gemm_i8_nogather).
+                     N>1: N-column split; each column sub-block is stored
+                     into the peers' C over NVLink (registered buffer) while
+                     the next is computed (zlift_part_gemm_ex_nsplit_overlap);
+                     also reported with an NCCL all-gather after the whole
+                     GEMM (gemm_i8_serialgather, zlift_part_gemm_ex_nsplit)
+                     and without any gather (gemm_i8_nogather).
   fmha               flash forward bf16 B=8 H=32 S=4096 D=128 causal, fp32
                      LSE; N>1: (batch, head) pairs split across GPUs
                      (zlift_part_flash_fwd), no collective.
@@ -341,9 +341,9 @@ class GemmI8(Workload):
         if not cls.gather:
             par = f"N-split x{world}, column blocks left on their GPUs"
         elif cls.overlap and world > 1:
-            par = (f"N-split x{world} in {sub_blocks_for(cls.N, world)} sub-blocks, NCCL "
-                   f"all-gather of each overlapping the next GEMM "
-                   f"(zlift_part_gemm_ex_nsplit_overlap)")
+            par = (f"N-split x{world} in {sub_blocks_for(cls.N, world)} sub-blocks, each "
+                   f"stored into the peers' C over NVLink while the next is computed "
+                   f"(zlift_part_gemm_ex_nsplit_overlap, registered C)")
         else:
             par = f"N-split x{world} + NCCL all-gather of C after the GEMM (zlift_part_gemm_ex_nsplit)"
         return {"workload": "cublasGemmEx int8->int32 M=2048 K=4096 N=14336 transa=T transb=N "
@@ -366,6 +366,10 @@ class GemmI8(Workload):
             box = [partition.Comm.unique_id() if rank == 0 else None]
             dist.broadcast_object_list(box, src=0)
             self.comm = partition.Comm(world, rank, box[0])
+            if self.overlap:
+                # the overlapped gather stores into the peers' C directly
+                rc = self.comm.register_peer_buffer(self.C, self.C.numel() * 4)
+                assert rc == 0, rc
         self.flops = 2.0 * self.M * self.N * self.K
         self.kernel_flops = 2.0 * self.M * self.nl * self.K
         self.kernel_bytes = float(self.M * self.K + self.K * self.nl + 4 * self.M * self.nl)
@@ -414,6 +418,10 @@ class GemmI8(Workload):
 
     def close(self):
         if self.comm is not None:
+            import torch
+            import torch.distributed as dist
+            torch.cuda.synchronize()
+            dist.barrier()                 # no rank still stores into another's C
             self.comm.close()
 
 

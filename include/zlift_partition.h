@@ -93,6 +93,24 @@ ZLIFT_API int zlift_part_gemm_ex_nsplit_overlap(
     const void *B_cols, int Btype, int ldb, const void *beta, void *C, int Ctype,
     int computeType);
 
+/* Maps a full-size output buffer C (`bytes` long, device memory of this
+ * rank) into every rank's address space (CUDA IPC, handles exchanged through
+ * the communicator) and gives it a flag array.  Collective: every rank calls
+ * it with its own C, the same `bytes`, before the first step that uses it.
+ * Afterwards zlift_part_gemm_ex_nsplit_overlap on this C gathers by storing
+ * each sub-block straight into the peers' C (a copy kernel on the
+ * communicator's second stream, next to the GEMM of the following
+ * sub-block) instead of through ncclAllGather; READY / DONE flags between
+ * the ranks order it, every wait bounded by the library's wait limit (a
+ * timeout is reported by zlift_device_error).  Up to 8 ranks.  0 success,
+ * 1 bad arguments, 13 a CUDA call failed, 100 + ncclResult_t. */
+ZLIFT_API int zlift_part_register_peer_buffer(void *comm, int nranks, int rank, void *C,
+                                             size_t bytes);
+/* Unmaps a registered C (after every rank's last use of it; waits for the
+ * device).  Also done for all of a communicator's buffers by
+ * zlift_part_comm_destroy.  1 if C was not registered. */
+ZLIFT_API int zlift_part_unregister_peer_buffer(void *comm, void *C);
+
 /* Attention forward restricted to (batch, head) pairs [pair_begin,
  * pair_end) in batch-major order, on `stream` (parameter block as for
  * zlift_flash_fwd).  0 done, 1 declined, 2 launch failure. */

@@ -3,9 +3,10 @@
 One process per GPU (spawned here), NCCL communicator created by the
 library (zlift_part_unique_id / zlift_part_comm_init; the id travels over a
 gloo process group):
-  - int8 N-split GEMM + all-gather, with the gather after the GEMM and
-    overlapped with it sub-block by sub-block: every rank's gathered C
-    equals the single-GPU product bit for bit;
+  - int8 N-split GEMM + all-gather, with the gather after the GEMM,
+    overlapped with it sub-block by sub-block (NCCL), and by peer stores into
+    a registered C (three steps in a row): every rank's gathered C equals
+    the single-GPU product bit for bit;
   - flash forward split by (batch, head) pairs: each rank's pairs equal the
     single-GPU result bit for bit (same kernel, same tiles).
 """
@@ -79,6 +80,24 @@ def _worker(rank, world, port, out):
         assert comm.wait(stream, 30000) == 0
         torch.cuda.synchronize()
         ok_gemm = ok_gemm and bool(torch.equal(C2, ref))
+        # ---- the same, gathered by peer stores into a registered C, three
+        # steps in a row with different B (epochs advance, C is reused) ----
+        C3 = torch.full((N, M), -1, dtype=torch.int32, device="cuda")
+        assert comm.register_peer_buffer(C3, C3.numel() * 4) == 0
+        for step in range(3):
+            Bs = torch.randint(-127, 128, (N, K), generator=g, device="cuda", dtype=torch.int8)
+            Bc = torch.cat([Bs[b:e] for b, e in cols]).contiguous()
+            st = partition.gemm_ex_nsplit_overlap(h, comm, world, rank, SB, 1, 0, M, N, K, 1, A,
+                                                  3, K, Bc, 3, K, 0, C3, 10, 72)
+            assert st == 0, st
+            ref3 = torch.empty_like(C3)
+            assert h.gemm_ex(1, 0, M, N, K, 1, A, 3, K, Bs, 3, K, 0, ref3, 10, M,
+                             compute=72) == 0
+            torch.cuda.synchronize()
+            ok_gemm = ok_gemm and bool(torch.equal(C3, ref3))
+        torch.cuda.synchronize()
+        dist.barrier()
+        assert comm.unregister_peer_buffer(C3) == 0
         # ---- attention split by (batch, head) ----
         Bq, S, H, D = 2, 512, 4, 128
         q = torch.randn(Bq, S, H, D, generator=g, device="cuda").bfloat16()

@@ -92,6 +92,8 @@ SIGNATURES = [
                                                   c_int, c_int, c_int, c_int, c_void_p, c_void_p,
                                                   c_int, c_int, c_void_p, c_int, c_int, c_void_p,
                                                   c_void_p, c_int, c_int]),
+    ("zlift_part_register_peer_buffer", c_int, [c_void_p, c_int, c_int, c_void_p, c_size_t]),
+    ("zlift_part_unregister_peer_buffer", c_int, [c_void_p, c_void_p]),
     ("zlift_part_flash_fwd", c_int, [c_void_p, c_uint, c_int, c_ll, c_ll, c_void_p]),
 ]
 

@@ -777,7 +777,8 @@ int zlift_device_error(void) {
     int e = gemm_tc_error(true);
     int e2 = gemm_simt_error(true);
     int e3 = fmha_error(true);
-    return e ? e : (e2 ? e2 : e3);
+    int e4 = part_error(true);
+    return e ? e : (e2 ? e2 : (e3 ? e3 : e4));
 }
 
 unsigned long long zlift_launch_count(void) { return launch_count(); }
@@ -785,7 +786,7 @@ unsigned long long zlift_launch_count(void) { return launch_count(); }
 int zlift_set_wait_limit_ns(unsigned long long ns) {
     if (ns == 0) return CUBLAS_STATUS_INVALID_VALUE;
     const int r = gemm_tc_set_wait_limit(ns) | gemm_simt_set_wait_limit(ns) |
-                  fmha_set_wait_limit(ns);
+                  fmha_set_wait_limit(ns) | part_set_wait_limit(ns);
     return r ? CUBLAS_STATUS_EXECUTION_FAILED : CUBLAS_STATUS_SUCCESS;
 }
 

@@ -111,6 +111,8 @@ int gemm_tc_error(bool clear);
 int gemm_tc_set_wait_limit(unsigned long long ns);
 int gemm_simt_set_wait_limit(unsigned long long ns);
 int fmha_set_wait_limit(unsigned long long ns);
+int part_error(bool clear);
+int part_set_wait_limit(unsigned long long ns);
 unsigned long long wait_limit_ns();
 // Launches a one-thread kernel whose mbarrier wait nobody completes: it
 // gives up after limit_ns, records kErrWaitTimeout and returns.

@@ -6,10 +6,12 @@
 // handle's stream so it follows the GEMM without a host round trip.
 #include "fmha.h"
 #include "gemm.h"
+#include "ptx.cuh"
 
 #include "../../include/zlift_cublas.h"
 #include "../../include/zlift_partition.h"
 
+#include <cuda.h>
 #include <dlfcn.h>
 
 #include <chrono>
@@ -129,7 +131,169 @@ void release_overlap(void* comm) {
     g_overlap.erase(it);
 }
 
+// ---- peer-memory gather (registered output buffers) ------------------------
+//
+// A registered C is mapped into every rank's address space (CUDA IPC); each
+// rank then writes its column sub-blocks straight into the peers' C -- by
+// copy-engine copies (cudaMemcpyAsync to the mapped peer address, one per
+// peer and sub-block) or by a store kernel -- on the communicator's second
+// stream, next to its own GEMM of the following sub-block, instead of an
+// ncclAllGather.  Two flags per
+// (step, source rank) in each rank's small flag array order it: READY (this
+// rank's stream has reached the call, so its C may be overwritten) and DONE
+// (the source has stored everything it owes this rank).  Every wait is
+// bounded by the library's wait limit and records kErrWaitTimeout.
+
+constexpr int kMaxRanks = 8;
+enum { kReady = 0, kDone = 1 };
+
+struct PeerPtrs {
+    uint4* dst[kMaxRanks];                  // peer copies of the same block (null: none)
+    unsigned long long* flag[kMaxRanks];    // peer's flag word for this rank (null: self)
+};
+
+// flags[kind * kMaxRanks + source]: epoch of the last signal from `source`
+__device__ __forceinline__ bool wait_flags(const volatile unsigned long long* flags, int kind,
+                                           int nranks, int self, unsigned long long epoch) {
+    const unsigned long long t0 = zl::globaltimer();
+    for (int r = 0; r < nranks; r++) {
+        if (r == self) continue;
+        uint32_t spins = 0;
+        while (flags[kind * kMaxRanks + r] < epoch) {
+            if ((++spins & 255u) == 0 && zl::globaltimer() - t0 > zl::g_wait_limit_ns) {
+                atomicCAS(&zl::g_dev_error, 0, (int)zl::kErrWaitTimeout);
+                return false;
+            }
+        }
+    }
+    __threadfence_system();
+    return true;
+}
+
+// One thread per peer: publish `epoch` in the peer's flag slot for this rank,
+// after everything this GPU wrote before (fence at system scope).
+__global__ void signal_peers_kernel(PeerPtrs pp, int nranks, unsigned long long epoch) {
+    const int r = threadIdx.x;
+    if (r >= nranks || !pp.flag[r]) return;
+    __threadfence_system();
+    *reinterpret_cast<volatile unsigned long long*>(pp.flag[r]) = epoch;
+    __threadfence_system();
+}
+
+// Copies n16 16-byte words of this rank's block into every peer's C (the
+// same offset), once every peer has signalled READY for `epoch`.
+__global__ void __launch_bounds__(512) push_block_kernel(const uint4* __restrict__ src,
+                                                         PeerPtrs pp, size_t n16, int nranks,
+                                                         int self,
+                                                         const unsigned long long* flags,
+                                                         unsigned long long epoch) {
+    __shared__ int go;
+    if (threadIdx.x == 0) go = wait_flags(flags, kReady, nranks, self, epoch) ? 1 : 0;
+    __syncthreads();
+    if (!go) return;
+    // four 16-byte words in flight per thread
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    for (; i + 3 * stride < n16; i += 4 * stride) {
+        uint4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) v[u] = src[i + u * stride];
+#pragma unroll
+        for (int r = 0; r < kMaxRanks; r++)
+            if (pp.dst[r]) {
+#pragma unroll
+                for (int u = 0; u < 4; u++) pp.dst[r][i + u * stride] = v[u];
+            }
+    }
+    for (; i < n16; i += stride) {
+        const uint4 v = src[i];
+#pragma unroll
+        for (int r = 0; r < kMaxRanks; r++)
+            if (pp.dst[r]) pp.dst[r][i] = v;
+    }
+    __threadfence_system();
+}
+
+// Waits (one thread) until every peer has signalled DONE (or READY) for `epoch`.
+__global__ void wait_flags_kernel(const unsigned long long* flags, int kind, int nranks,
+                                  int self, unsigned long long epoch) {
+    if (threadIdx.x == 0) wait_flags(flags, kind, nranks, self, epoch);
+}
+
+struct PeerBuf {
+    int nranks = 0, rank = 0, device = -1;
+    char* C = nullptr;
+    size_t bytes = 0;
+    char* peer_C[kMaxRanks] = {};              // peers' C in this address space (self: C)
+    void* peer_base[kMaxRanks] = {};           // opened IPC mappings of C's allocation
+    unsigned long long* flags = nullptr;       // this rank's [2][kMaxRanks] flag words
+    unsigned long long* peer_flags[kMaxRanks] = {};   // peers' flag arrays
+    unsigned long long epoch = 0;
+};
+std::mutex g_peer_mu;
+std::map<std::pair<void*, void*>, PeerBuf> g_peer;     // (comm, C)
+
+using AddrRangeFn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+AddrRangeFn addr_range_fn() {
+    static AddrRangeFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &f, cudaEnableDefault, &q) ==
+                cudaSuccess && q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<AddrRangeFn>(f);
+        else
+            cudaGetLastError();
+    });
+    return fn;
+}
+
+void close_peer_buf(PeerBuf& b) {
+    int cur = 0;
+    cudaGetDevice(&cur);
+    cudaSetDevice(b.device);
+    for (int r = 0; r < kMaxRanks; r++) {
+        if (b.peer_base[r]) cudaIpcCloseMemHandle(b.peer_base[r]);
+        if (b.peer_flags[r] && r != b.rank) cudaIpcCloseMemHandle(b.peer_flags[r]);
+    }
+    if (b.flags) cudaFree(b.flags);
+    cudaGetLastError();
+    cudaSetDevice(cur);
+}
+
+void release_peer_bufs(void* comm) {
+    std::lock_guard<std::mutex> lock(g_peer_mu);
+    for (auto it = g_peer.begin(); it != g_peer.end();) {
+        if (it->first.first == comm) {
+            close_peer_buf(it->second);
+            it = g_peer.erase(it);
+        } else {
+            ++it;
+        }
+    }
+}
+
+PeerBuf* find_peer_buf(void* comm, void* C) {
+    std::lock_guard<std::mutex> lock(g_peer_mu);
+    auto it = g_peer.find({comm, C});
+    return it == g_peer.end() ? nullptr : &it->second;
+}
+
 }  // namespace
+
+namespace zl {
+int part_error(bool clear) {
+    int v = 0;
+    cudaMemcpyFromSymbol(&v, g_dev_error, sizeof(int));
+    if (clear && v) {
+        int z = 0;
+        cudaMemcpyToSymbol(g_dev_error, &z, sizeof(int));
+    }
+    return v;
+}
+int part_set_wait_limit(unsigned long long ns) { return set_unit_wait_limit(ns); }
+}  // namespace zl
 
 extern "C" {
 
@@ -176,6 +340,7 @@ int zlift_part_comm_destroy(void* comm) {
     const Nccl& n = nccl();
     if (!n.ok || !comm) return 1;
     release_overlap(comm);
+    release_peer_bufs(comm);
     NcclResult r = n.comm_destroy(comm);
     return r == kNcclSuccess ? 0 : 100 + r;
 }
@@ -193,6 +358,7 @@ int zlift_part_comm_wait(void* comm, void* stream, int timeout_ms) {
         if (err != kNcclSuccess && err != kNcclInProgress) {
             n.comm_abort(comm);
             release_overlap(comm);
+            release_peer_bufs(comm);
             return 100 + err;
         }
         const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(
@@ -200,6 +366,7 @@ int zlift_part_comm_wait(void* comm, void* stream, int timeout_ms) {
         if (ms > timeout_ms) {
             n.comm_abort(comm);
             release_overlap(comm);
+            release_peer_bufs(comm);
             return 200;
         }
         std::this_thread::sleep_for(std::chrono::microseconds(200));
@@ -273,6 +440,103 @@ int zlift_part_gemm_ex_nsplit(void* handle, void* comm, int nranks, int rank, in
     return r == kNcclSuccess ? 0 : 100 + r;
 }
 
+int zlift_part_register_peer_buffer(void* comm, int nranks, int rank, void* C, size_t bytes) {
+    const Nccl& nc = nccl();
+    if (!nc.ok || !comm || !C || bytes == 0 || nranks <= 1 || nranks > kMaxRanks || rank < 0 ||
+        rank >= nranks)
+        return 1;
+    if (find_peer_buf(comm, C)) return 0;                 // already registered
+    AddrRangeFn range = addr_range_fn();
+    if (!range) return 1;
+    CUdeviceptr base = 0;
+    size_t alloc = 0;
+    if (range(&base, &alloc, reinterpret_cast<CUdeviceptr>(C)) != CUDA_SUCCESS) return 1;
+    const unsigned long long off = reinterpret_cast<CUdeviceptr>(C) - base;
+    if (off + bytes > alloc) return 1;
+    struct Info {
+        cudaIpcMemHandle_t c, f;
+        unsigned long long off, bytes;
+    };
+    PeerBuf b;
+    b.nranks = nranks;
+    b.rank = rank;
+    cudaGetDevice(&b.device);
+    b.C = static_cast<char*>(C);
+    b.bytes = bytes;
+    Info mine{};
+    int rc = 0;
+    if (cudaMalloc(&b.flags, 2 * kMaxRanks * sizeof(unsigned long long)) != cudaSuccess ||
+        cudaMemset(b.flags, 0, 2 * kMaxRanks * sizeof(unsigned long long)) != cudaSuccess ||
+        cudaIpcGetMemHandle(&mine.c, reinterpret_cast<void*>(base)) != cudaSuccess ||
+        cudaIpcGetMemHandle(&mine.f, b.flags) != cudaSuccess)
+        rc = 13;
+    mine.off = off;
+    mine.bytes = bytes;
+    // exchange the handles through the communicator (in-place all-gather of
+    // one Info per rank), then open every peer's mappings
+    Info* dinfo = nullptr;
+    cudaStream_t st = nullptr;
+    std::vector<Info> all(nranks);
+    if (cudaMalloc(&dinfo, sizeof(Info) * nranks) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking) != cudaSuccess) {
+        rc = 13;
+    } else if (cudaMemset(dinfo, 0, sizeof(Info) * nranks) != cudaSuccess ||
+               (rc == 0 && cudaMemcpy(dinfo + rank, &mine, sizeof(Info),
+                                      cudaMemcpyHostToDevice) != cudaSuccess)) {
+        rc = 13;
+    }
+    // every rank takes part in the all-gather, even one that failed above (it
+    // sends zeros and then reports its error), so no rank waits for it
+    if (dinfo && st) {
+        NcclResult r = nc.all_gather(dinfo + rank, dinfo, sizeof(Info), kNcclInt8, comm, st);
+        if (r != kNcclSuccess && rc == 0) rc = 100 + r;
+        if (cudaStreamSynchronize(st) != cudaSuccess && rc == 0) rc = 13;
+        if (cudaMemcpy(all.data(), dinfo, sizeof(Info) * nranks, cudaMemcpyDeviceToHost) !=
+                cudaSuccess && rc == 0)
+            rc = 13;
+    }
+    if (st) cudaStreamDestroy(st);
+    if (dinfo) cudaFree(dinfo);
+    for (int p = 0; rc == 0 && p < nranks; p++) {
+        if (p == rank) {
+            b.peer_C[p] = b.C;
+            continue;
+        }
+        if (all[p].bytes != bytes) { rc = 1; break; }
+        void* pb = nullptr;
+        void* pf = nullptr;
+        if (cudaIpcOpenMemHandle(&pb, all[p].c, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            rc = 13;
+            break;
+        }
+        b.peer_base[p] = pb;
+        if (cudaIpcOpenMemHandle(&pf, all[p].f, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            rc = 13;
+            break;
+        }
+        b.peer_flags[p] = static_cast<unsigned long long*>(pf);
+        b.peer_C[p] = static_cast<char*>(pb) + all[p].off;
+    }
+    if (rc) {
+        cudaGetLastError();
+        close_peer_buf(b);
+        return rc;
+    }
+    std::lock_guard<std::mutex> lock(g_peer_mu);
+    g_peer[{comm, C}] = b;
+    return 0;
+}
+
+int zlift_part_unregister_peer_buffer(void* comm, void* C) {
+    std::lock_guard<std::mutex> lock(g_peer_mu);
+    auto it = g_peer.find({comm, C});
+    if (it == g_peer.end()) return 1;
+    cudaDeviceSynchronize();
+    close_peer_buf(it->second);
+    g_peer.erase(it);
+    return 0;
+}
+
 int zlift_part_nsplit_cols(long long n, int nranks, int rank, int sub_blocks, int s,
                            long long* begin, long long* end) {
     if (!begin || !end || n <= 0 || nranks <= 0 || rank < 0 || rank >= nranks || sub_blocks <= 0 ||
@@ -321,13 +585,93 @@ int zlift_part_gemm_ex_nsplit_overlap(void* handle, void* comm, int nranks, int 
     if (!nc.ok || !comm) return 1;
     Overlap* ov = overlap_for(comm, sub_blocks);
     if (!ov) return 1;
-    // leave SMs to NCCL's kernels, which run next to the GEMMs
+    // a registered C (zlift_part_register_peer_buffer) is gathered by peer
+    // stores, else by NCCL
+    PeerBuf* pbuf = find_peer_buf(comm, C);
+    const size_t sub_bytes = (size_t)w * (size_t)m * es;
+    if (pbuf && (pbuf->nranks != nranks || pbuf->rank != rank || sub_bytes % 16 ||
+                 (reinterpret_cast<uintptr_t>(C) & 15) ||
+                 (size_t)n * (size_t)m * es > pbuf->bytes))
+        pbuf = nullptr;
+    // registered C: the sub-blocks go to the peers by copy-engine copies
+    // (default; no SM is taken from the GEMM) or by a store kernel
+    // (ZLIFT_PART_GATHER=sm, ZLIFT_PART_PUSH_SMS CTAs)
+    const char* gmode = getenv("ZLIFT_PART_GATHER");
+    const bool by_ce = pbuf && !(gmode && gmode[0] == 's');
+    // leave SMs to the gather's kernels, which run next to the GEMMs
     int target = 0;
     cublasGetSmCountTarget(handle, &target);
-    int reserve = 16;
-    if (const char* e = getenv("ZLIFT_PART_COMM_SMS")) reserve = atoi(e);
+    int reserve = pbuf ? (by_ce ? 0 : 32) : 16;
+    if (const char* e = getenv(pbuf ? "ZLIFT_PART_PUSH_SMS" : "ZLIFT_PART_COMM_SMS"))
+        if (!by_ce) reserve = atoi(e);
     const int sms = zl::num_sms();
     if (reserve > 0 && reserve < sms) cublasSetSmCountTarget(handle, sms - reserve);
+    if (pbuf) {
+        const unsigned long long epoch = ++pbuf->epoch;
+        PeerPtrs sig{};
+        for (int r = 0; r < nranks; r++)
+            if (r != rank) sig.flag[r] = pbuf->peer_flags[r] + kReady * kMaxRanks + rank;
+        // this rank's C may be overwritten once its stream has reached here
+        signal_peers_kernel<<<1, 32, 0, s>>>(sig, nranks, epoch);
+        int rc = cudaGetLastError() == cudaSuccess ? 0 : 13;
+        const int ctas = reserve > 0 && reserve < sms ? reserve : 16;
+        bool ready_waited = false;
+        for (int sb = 0; sb < sub_blocks && rc == 0; sb++) {
+            zlift_part_nsplit_cols(n, nranks, rank, sub_blocks, sb, &c0, &c1);
+            const size_t off = (size_t)c0 * (size_t)m * es;
+            rc = cublasGemmEx(handle, transa, transb, m, (int)w, k, alpha, A, Atype, lda,
+                              static_cast<const char*>(B_cols) + sb * b_step * bes, Btype, ldb,
+                              beta, pbuf->C + off, Ctype, m, computeType, 0);
+            if (rc) break;
+            if (cudaEventRecord(ov->gemm_done[sb], s) != cudaSuccess ||
+                cudaStreamWaitEvent(ov->stream, ov->gemm_done[sb], 0) != cudaSuccess) {
+                rc = 13;
+                break;
+            }
+            if (by_ce) {
+                // the copies may start once every peer is READY (one wait per call)
+                if (!ready_waited) {
+                    wait_flags_kernel<<<1, 32, 0, ov->stream>>>(pbuf->flags, kReady, nranks, rank,
+                                                               epoch);
+                    if (cudaGetLastError() != cudaSuccess) { rc = 13; break; }
+                    zl::note_launch();
+                    ready_waited = true;
+                }
+                for (int r = 0; r < nranks && rc == 0; r++) {
+                    if (r == rank) continue;
+                    if (cudaMemcpyAsync(pbuf->peer_C[r] + off, pbuf->C + off, sub_bytes,
+                                        cudaMemcpyDeviceToDevice, ov->stream) != cudaSuccess)
+                        rc = 13;
+                }
+                continue;
+            }
+            PeerPtrs pp{};
+            for (int r = 0; r < nranks; r++)
+                if (r != rank) pp.dst[r] = reinterpret_cast<uint4*>(pbuf->peer_C[r] + off);
+            push_block_kernel<<<ctas, 512, 0, ov->stream>>>(
+                reinterpret_cast<const uint4*>(pbuf->C + off), pp, sub_bytes / 16, nranks, rank,
+                pbuf->flags, epoch);
+            if (cudaGetLastError() != cudaSuccess) rc = 13;
+            else zl::note_launch();
+        }
+        cublasSetSmCountTarget(handle, target);
+        // tell every peer that all of its columns from this rank have landed
+        PeerPtrs done{};
+        for (int r = 0; r < nranks; r++)
+            if (r != rank) done.flag[r] = pbuf->peer_flags[r] + kDone * kMaxRanks + rank;
+        signal_peers_kernel<<<1, 32, 0, ov->stream>>>(done, nranks, epoch);
+        if (cudaGetLastError() != cudaSuccess && rc == 0) rc = 13;
+        // the handle's stream continues once this rank's stores are out and
+        // every peer's have arrived
+        if (cudaEventRecord(ov->gathered, ov->stream) != cudaSuccess ||
+            cudaStreamWaitEvent(s, ov->gathered, 0) != cudaSuccess) {
+            if (rc == 0) rc = 13;
+        }
+        wait_flags_kernel<<<1, 32, 0, s>>>(pbuf->flags, kDone, nranks, rank, epoch);
+        if (cudaGetLastError() != cudaSuccess && rc == 0) rc = 13;
+        zl::note_launch(3);
+        return rc;
+    }
     const int dt = Ctype == zl::kR32I ? kNcclInt32 : kNcclInt8;
     const size_t unit = Ctype == zl::kR32I ? 1 : (size_t)es;
     int rc = 0;

@@ -102,6 +102,17 @@ class Comm:
             self.c = None
         return rc
 
+    def register_peer_buffer(self, C, nbytes: int) -> int:
+        """Collective: maps C into every rank (zlift_part_register_peer_buffer),
+        so the overlapped N-split gathers into it by peer stores."""
+        from .blas import _ptr
+        return self.lib.zlift_part_register_peer_buffer(self.c, self.nranks, self.rank, _ptr(C),
+                                                        nbytes)
+
+    def unregister_peer_buffer(self, C) -> int:
+        from .blas import _ptr
+        return self.lib.zlift_part_unregister_peer_buffer(self.c, _ptr(C))
+
     def close(self):
         if self.c:
             self.lib.zlift_part_comm_destroy(self.c)
