@@ -71,6 +71,9 @@ struct TcParams {
     // u); each later tile is split along K into `split` units.  split == 1:
     // main_units = total_units = number of tiles.
     int main_units, total_units, split;
+    // tail_halves: the tiles after main_units are each two units of BN/2
+    // columns (an N split of a sparse last wave) instead of K-split parts
+    int tail_halves;
     int kc;                          // K blocks per accumulation chunk (see fold_chunks)
     uint32_t* work;                  // partial sums of split tiles (fp32 or int32 bits)
     size_t work_bytes;
@@ -79,18 +82,27 @@ struct TcParams {
 };
 
 // What one unit of work covers: output tile `t` and K blocks [kb0, kb1);
-// part >= 0 for a K-split unit.
+// part >= 0 for a K-split unit; nh = 1 or 2 for the first or second
+// BN/2-column half of a tile (0: the whole tile).
 struct Unit {
-    int t, kb0, kb1, part;
+    int t, kb0, kb1, part, nh;
 };
 
 __device__ __forceinline__ Unit unit_of(const TcParams& p, int u) {
     Unit r;
+    r.nh = 0;
     if (u < p.main_units) {
         r.t = u;
         r.kb0 = 0;
         r.kb1 = p.k_blocks;
         r.part = -1;
+    } else if (p.tail_halves) {
+        const int v = u - p.main_units;
+        r.t = p.main_units + v / 2;
+        r.kb0 = 0;
+        r.kb1 = p.k_blocks;
+        r.part = -1;
+        r.nh = 1 + (v & 1);
     } else {
         const int v = u - p.main_units;
         const int s = v % p.split;
@@ -547,6 +559,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
     constexpr int KSTEPS = BK / UK;
     constexpr uint32_t IDESC =
         make_idesc(KT<KIND>::cfmt, KT<KIND>::abfmt, A_MN ? 1 : 0, B_MN ? 1 : 0, TILE_M, BN);
+    // half-width units of a split last wave: the same loads, N = BN/2
+    constexpr uint32_t IDESC_HALF =
+        make_idesc(KT<KIND>::cfmt, KT<KIND>::abfmt, A_MN ? 1 : 0, B_MN ? 1 : 0, TILE_M, BN / 2);
     constexpr uint32_t TMEM_COLS = C_::TMEM_COLS;
     constexpr bool CHUNKED = KIND == (int)Kind::TF32X3;
 
@@ -621,7 +636,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                 int b, tm, tn;
                 decode_tile(un.t, p.tiles_m, p.tiles_n, b, tm, tn);
                 const int m0 = tm * TILE_M + (int)rank * BM;
-                const int n0 = tn * BN + (int)rank * B_ROWS;
+                // a half unit loads the full box from its half's first column
+                // (each CTA of a pair from its quarter); the MMA reads the
+                // leading BN/2 (or BN/4) columns
+                const int n0 = tn * BN + (un.nh ? (un.nh - 1) * (BN / 2) : 0) +
+                               (int)rank * (un.nh ? B_ROWS / 2 : B_ROWS);
                 for (int kb = un.kb0; kb < un.kb1; kb++) {
                     if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) goto producer_done;
                     uint8_t* sa = smem + stage * STAGE_BYTES;
@@ -665,6 +684,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
             // unless the kernel accumulates in chunks)
             for (int u = cta_id; u < total; u += n_ctas) {
                 const Unit un = unit_of(p, u);
+                const uint32_t idesc = un.nh ? IDESC_HALF : IDESC;
                 for (int c0 = un.kb0; c0 < un.kb1; c0 += p.kc, local++) {
                 const int c1 = min(c0 + p.kc, un.kb1);
                 const int acc = local & 1;
@@ -686,17 +706,17 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                             // small terms first: lo*hi, hi*lo, then hi*hi
                             const uint64_t ad2 = operand_desc<A_MN, BK, UK>(sb + B_BYTES, ks);
                             const uint64_t bd2 = operand_desc<B_MN, BK, UK>(sb + B_BYTES + A_BYTES, ks);
-                            mma_tf32_ss(d, ad2, bd, IDESC, accum);
-                            mma_tf32_ss(d, ad, bd2, IDESC, 1u);
-                            mma_tf32_ss(d, ad, bd, IDESC, 1u);
+                            mma_tf32_ss(d, ad2, bd, idesc, accum);
+                            mma_tf32_ss(d, ad, bd2, idesc, 1u);
+                            mma_tf32_ss(d, ad, bd, idesc, 1u);
                         } else if constexpr (KIND == (int)Kind::TF32) {
-                            mma_tf32_ss(d, ad, bd, IDESC, accum);
+                            mma_tf32_ss(d, ad, bd, idesc, accum);
                         } else if constexpr (KIND == (int)Kind::I8) {
-                            if constexpr (PAIR) mma_i8_ss_pair(d, ad, bd, IDESC, accum);
-                            else mma_i8_ss(d, ad, bd, IDESC, accum);
+                            if constexpr (PAIR) mma_i8_ss_pair(d, ad, bd, idesc, accum);
+                            else mma_i8_ss(d, ad, bd, idesc, accum);
                         } else {
-                            if constexpr (PAIR) mma_f16_ss_pair(d, ad, bd, IDESC, accum);
-                            else mma_f16_ss(d, ad, bd, IDESC, accum);
+                            if constexpr (PAIR) mma_f16_ss_pair(d, ad, bd, idesc, accum);
+                            else mma_f16_ss(d, ad, bd, idesc, accum);
                         }
                     }
                     if constexpr (PAIR) mma_commit_pair(&empty[stage], 0x3);
@@ -770,9 +790,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                 }
                 int b, tm, tn;
                 decode_tile(un.t, p.tiles_m, p.tiles_n, b, tm, tn);
-                const int m0 = tm * TILE_M + (int)rank * BM, n0 = tn * BN;
+                const int width = un.nh ? BN / 2 : BN;      // columns of this unit
+                const int m0 = tm * TILE_M + (int)rank * BM,
+                          n0 = tn * BN + (un.nh ? (un.nh - 1) * (BN / 2) : 0);
                 const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
-                const int ncols = min(BN, p.n - n0);
+                const int ncols = min(width, p.n - n0);
                 const float bias_row = load_bias(p, (long long)m0 + r_in_tile);
                 if (un.part >= 0) {             // K-split unit: out of line
                     SplitArgs sa;
@@ -918,7 +940,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                 decode_tile(un.t, p.tiles_m, p.tiles_n, b, tm, tn);
                 const long long row = (long long)tm * TILE_M + (int)rank * BM + r_in_tile;
                 const bool row_ok = row < p.m;
-                const int n0 = tn * BN;
+                const int width = un.nh ? BN / 2 : BN;      // columns of this unit
+                const int n0 = tn * BN + (un.nh ? (un.nh - 1) * (BN / 2) : 0);
+                const int nlim = min(p.n, n0 + width);
                 const long long base = (long long)b * p.strideC + row;
                 const float bias_row = load_bias(p, row);
                 const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
@@ -930,16 +954,16 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
 #pragma unroll
                     for (int j = 0; j < 32; j++) {
                         const int col = n0 + c0 + j;
-                        dst[j] = (use_beta && row_ok && col < p.n)
+                        dst[j] = (use_beta && row_ok && col < nlim)
                                      ? load_c<OUT>(p.C, base + (long long)col * p.ldc) : 0u;
                     }
                 };
                 fetch(0, old);
 #pragma unroll 1
-                for (int c0 = 0; c0 < BN; c0 += 32) {
+                for (int c0 = 0; c0 < width; c0 += 32) {
                     uint32_t v[32];
                     tmem_ld32(taddr + c0, v);
-                    if (c0 + 32 < BN) fetch(c0 + 32, old_next);
+                    if (c0 + 32 < width) fetch(c0 + 32, old_next);
                     tmem_wait_ld();
                     // the activation branch outside the unrolled loop (see
                     // convert_chunk_t): epi == 0 compiles to no activation code
@@ -947,7 +971,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
 #pragma unroll
                         for (int j = 0; j < 32; j++) {
                             const int col = n0 + c0 + j;
-                            if (col < p.n)
+                            if (col < nlim)
                                 store_out<OUT>(p.C, base + (long long)col * p.ldc, v[j], old[j],
                                                use_beta, alpha, beta, ia, ib, p.epi, bias_row);
                         }
@@ -955,7 +979,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
 #pragma unroll
                         for (int j = 0; j < 32; j++) {
                             const int col = n0 + c0 + j;
-                            if (col < p.n)
+                            if (col < nlim)
                                 store_out<OUT>(p.C, base + (long long)col * p.ldc, v[j], old[j],
                                                use_beta, alpha, beta, ia, ib, 0, 0.f);
                         }
@@ -1093,9 +1117,25 @@ constexpr bool pair_ok(int kind, int bn) {
 // completes a tile stages the other S-1 parts' 16 KB column chunks in the
 // operand ring (`ring_bytes`), so S-1 chunks must fit there.  Without a
 // workspace large enough, nothing is split.
-void split_tail(TcParams& q, int tiles, int slots, size_t unit_bytes, size_t ring_bytes) {
+void split_tail(TcParams& q, int tiles, int slots, size_t unit_bytes, size_t ring_bytes,
+                bool halves_ok) {
     q.main_units = q.total_units = tiles;
     q.split = 1;
+    q.tail_halves = 0;
+    // A last wave after full waves that fills at most half of the CTAs:
+    // each of its tiles becomes two half-width units, so the wave takes
+    // about half a tile's time (no partial sums to combine).
+    // ZBLAS_TAIL_HALVES=0 turns it off.
+    {
+        const char* th = getenv("ZBLAS_TAIL_HALVES");
+        const int rem = slots > 0 ? tiles % slots : 0;
+        if (halves_ok && !(th && th[0] == '0') && tiles >= slots && rem > 0 && 2 * rem <= slots) {
+            q.tail_halves = 1;
+            q.main_units = tiles - rem;
+            q.total_units = tiles + rem;
+            return;
+        }
+    }
     // ZBLAS_SPLIT_K: unset = split only a GEMM that is one sparse wave (fewer
     // tiles than half the CTAs: small m x n, long k); 1 = also the sparse
     // last wave after full waves (measured slower on 4096^3); 0 = never
@@ -1160,8 +1200,13 @@ int launch_one(const Maps& m, const TcParams& p, cudaStream_t s) {
     if (m.sm_limit > 0) slots = std::min(slots, PAIR ? std::max(1, m.sm_limit / 2) : m.sm_limit);
     TcParams q = p;
     const int tiles = p.tiles_m * p.tiles_n * p.batch;
+    // half units: each CTA's share of a half (BN/2, or BN/4 for a pair) must
+    // be whole swizzle rows of an MN-major B tile
+    constexpr int kHalfCols = PAIR ? BN / 4 : BN / 2;
+    constexpr bool kHalvesOk = KIND != (int)Kind::TF32X3 && BN >= 128 &&
+                               (!B_MN || kHalfCols % C_::BOX == 0);
     split_tail(q, tiles, slots, m.staged ? BN * BM * 4 * (PAIR ? 2 : 1) : 0,
-               (size_t)C_::STAGES * C_::STAGE_BYTES);
+               (size_t)C_::STAGES * C_::STAGE_BYTES, kHalvesOk);
     const int total = q.total_units;
     cudaError_t e;
     if constexpr (PAIR) {
@@ -1347,6 +1392,7 @@ int gemm_tc(const GemmDesc& d, cudaStream_t s) {
     p.epoch = d.split_epoch & 0xffffffffffffull;
     p.main_units = p.total_units = p.tiles_m * p.tiles_n * p.batch;
     p.split = 1;
+    p.tail_halves = 0;
     // 3xTF32: a fresh accumulator every 4 K blocks (128 of K)
     p.kc = d.kind == Kind::TF32X3 ? 4 : (p.k_blocks > 0 ? p.k_blocks : 1);
 
