@@ -17,12 +17,15 @@ those of gemm_f16, the configuration the metric is quoted on, and
                      alpha=1/sqrt(512), beta=0; N>1: batch split across GPUs
                      (zlift_part_gemm_strided_batched_ex), no collective.
   gemm_i8            cublasGemmEx int8 -> int32, M=2048 K=4096 N=14336, TN;
-                     N>1: N-column split; each column sub-block is stored
-                     into the peers' C over NVLink (registered buffer) while
-                     the next is computed (zlift_part_gemm_ex_nsplit_overlap);
-                     also reported with an NCCL all-gather after the whole
-                     GEMM (gemm_i8_serialgather, zlift_part_gemm_ex_nsplit)
-                     and without any gather (gemm_i8_nogather).
+                     N>1: N-column split and a gather of C, in the form
+                     measured fastest at that N: at N = 2 each column
+                     sub-block is copied into the peer's C by the copy
+                     engines while the next is computed (registered buffer,
+                     zlift_part_gemm_ex_nsplit_overlap), above that one NCCL
+                     all-gather after the GEMM (zlift_part_gemm_ex_nsplit);
+                     the other form is reported too (gemm_i8_serialgather at
+                     N = 2, gemm_i8_peercopy above), and the split without
+                     any gather (gemm_i8_nogather).
   fmha               flash forward bf16 B=8 H=32 S=4096 D=128 causal, fp32
                      LSE; N>1: (batch, head) pairs split across GPUs
                      (zlift_part_flash_fwd), no collective.
@@ -334,13 +337,20 @@ class GemmI8(Workload):
     peak_scale = 2.0
     M, K, N = 2048, 4096, 14336
     gather = True
-    overlap = True           # N > 1: all-gather overlapped with the GEMM, sub-block by sub-block
+    # N > 1: how C is gathered.  None = the form measured fastest at this N:
+    # copy-engine copies into the peers' C overlapped with the GEMM at N = 2,
+    # one NCCL all-gather after the GEMM above (see overlap_for)
+    overlap = None
+
+    @classmethod
+    def overlap_for(cls, world):
+        return (world == 2) if cls.overlap is None else cls.overlap
 
     @classmethod
     def config_for(cls, world):
         if not cls.gather:
             par = f"N-split x{world}, column blocks left on their GPUs"
-        elif cls.overlap and world > 1:
+        elif cls.overlap_for(world) and world > 1:
             par = (f"N-split x{world} in {sub_blocks_for(cls.N, world)} sub-blocks, each "
                    f"stored into the peers' C over NVLink while the next is computed "
                    f"(zlift_part_gemm_ex_nsplit_overlap, registered C)")
@@ -356,6 +366,7 @@ class GemmI8(Workload):
         import torch.distributed as dist
         from zlift_b200 import partition
         self.h, self.world, self.rank = h, world, rank
+        self.overlap = self.overlap_for(world)
         lo, hi = partition.shard_range(self.N, world, rank, align=128)
         self.n0, self.nl = lo, hi - lo
         self.A = _gen("i8", (self.M, self.K), 60, dev)                 # stored K x M (op T)
@@ -433,6 +444,11 @@ class GemmI8NoGather(GemmI8):
 class GemmI8SerialGather(GemmI8):
     name = "gemm_i8_serialgather"
     overlap = False
+
+
+class GemmI8PeerCopy(GemmI8):
+    name = "gemm_i8_peercopy"
+    overlap = True
 
 
 class Fmha(Workload):
@@ -561,7 +577,7 @@ class Sgemm(Workload):
 
 
 WORKLOADS = {w.name: w for w in (GemmF16, GemmBF16Batched, GemmI8, GemmI8NoGather,
-                                 GemmI8SerialGather, Fmha, Sgemm)}
+                                 GemmI8SerialGather, GemmI8PeerCopy, Fmha, Sgemm)}
 
 
 # --------------------------------------------------------------------------
@@ -851,8 +867,11 @@ def main(argv=None):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     names = ORDER if a.workload == "all" else [a.workload]
-    if a.workload == "all" and max(world, a.gpus) > 1:
-        names = names + ["gemm_i8_serialgather", "gemm_i8_nogather"]
+    nw = max(world, a.gpus)
+    if a.workload == "all" and nw > 1:
+        # the int8 gather form gemm_i8 does not use, and no gather at all
+        names = names + ["gemm_i8_serialgather" if nw == 2 else "gemm_i8_peercopy",
+                         "gemm_i8_nogather"]
     head = HEADLINE if HEADLINE in names else names[0]
 
     if a.impl == "reference":

@@ -87,6 +87,10 @@ struct Overlap {
     cudaStream_t stream = nullptr;
     std::vector<cudaEvent_t> gemm_done;
     cudaEvent_t gathered = nullptr;
+    // copy-engine gather: one stream per peer (copies to different peers
+    // run on different copy engines), each ending on its own event
+    cudaStream_t peer_stream[8] = {};
+    cudaEvent_t peer_done[8] = {};
 };
 std::mutex g_overlap_mu;
 std::map<void*, Overlap> g_overlap;
@@ -106,6 +110,15 @@ Overlap* overlap_for(void* comm, int sub_blocks) {
         o.device = dev;
     }
     if (o.device != dev) return nullptr;
+    if (!o.peer_stream[0]) {
+        for (int r = 0; r < 8; r++) {
+            if (cudaStreamCreateWithFlags(&o.peer_stream[r], cudaStreamNonBlocking) != cudaSuccess ||
+                cudaEventCreateWithFlags(&o.peer_done[r], cudaEventDisableTiming) != cudaSuccess) {
+                cudaGetLastError();
+                return nullptr;
+            }
+        }
+    }
     while ((int)o.gemm_done.size() < sub_blocks) {
         cudaEvent_t e;
         if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) {
@@ -127,6 +140,10 @@ void release_overlap(void* comm) {
     for (cudaEvent_t e : it->second.gemm_done) cudaEventDestroy(e);
     if (it->second.gathered) cudaEventDestroy(it->second.gathered);
     if (it->second.stream) cudaStreamDestroy(it->second.stream);
+    for (int r = 0; r < 8; r++) {
+        if (it->second.peer_done[r]) cudaEventDestroy(it->second.peer_done[r]);
+        if (it->second.peer_stream[r]) cudaStreamDestroy(it->second.peer_stream[r]);
+    }
     cudaSetDevice(cur);
     g_overlap.erase(it);
 }
@@ -629,7 +646,8 @@ int zlift_part_gemm_ex_nsplit_overlap(void* handle, void* comm, int nranks, int 
                 break;
             }
             if (by_ce) {
-                // the copies may start once every peer is READY (one wait per call)
+                // the copies may start once every peer is READY (one wait per
+                // call, on the second stream, which every peer stream follows)
                 if (!ready_waited) {
                     wait_flags_kernel<<<1, 32, 0, ov->stream>>>(pbuf->flags, kReady, nranks, rank,
                                                                epoch);
@@ -637,10 +655,17 @@ int zlift_part_gemm_ex_nsplit_overlap(void* handle, void* comm, int nranks, int 
                     zl::note_launch();
                     ready_waited = true;
                 }
+                if (cudaEventRecord(ov->gemm_done[sb], ov->stream) != cudaSuccess) {
+                    rc = 13;
+                    break;
+                }
                 for (int r = 0; r < nranks && rc == 0; r++) {
                     if (r == rank) continue;
-                    if (cudaMemcpyAsync(pbuf->peer_C[r] + off, pbuf->C + off, sub_bytes,
-                                        cudaMemcpyDeviceToDevice, ov->stream) != cudaSuccess)
+                    if (cudaStreamWaitEvent(ov->peer_stream[r], ov->gemm_done[sb], 0) !=
+                            cudaSuccess ||
+                        cudaMemcpyAsync(pbuf->peer_C[r] + off, pbuf->C + off, sub_bytes,
+                                        cudaMemcpyDeviceToDevice, ov->peer_stream[r]) !=
+                            cudaSuccess)
                         rc = 13;
                 }
                 continue;
@@ -655,6 +680,15 @@ int zlift_part_gemm_ex_nsplit_overlap(void* handle, void* comm, int nranks, int 
             else zl::note_launch();
         }
         cublasSetSmCountTarget(handle, target);
+        if (by_ce) {
+            // the DONE signal follows every peer stream's copies
+            for (int r = 0; r < nranks && rc == 0; r++) {
+                if (r == rank) continue;
+                if (cudaEventRecord(ov->peer_done[r], ov->peer_stream[r]) != cudaSuccess ||
+                    cudaStreamWaitEvent(ov->stream, ov->peer_done[r], 0) != cudaSuccess)
+                    rc = 13;
+            }
+        }
         // tell every peer that all of its columns from this rank have landed
         PeerPtrs done{};
         for (int r = 0; r < nranks; r++)
