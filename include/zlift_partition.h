@@ -96,14 +96,19 @@ ZLIFT_API int zlift_part_gemm_ex_nsplit_overlap(
 /* Maps a full-size output buffer C (`bytes` long, device memory of this
  * rank) into every rank's address space (CUDA IPC, handles exchanged through
  * the communicator) and gives it a flag array.  Collective: every rank calls
- * it with its own C, the same `bytes`, before the first step that uses it.
- * Afterwards zlift_part_gemm_ex_nsplit_overlap on this C gathers by storing
- * each sub-block straight into the peers' C (a copy kernel on the
- * communicator's second stream, next to the GEMM of the following
- * sub-block) instead of through ncclAllGather; READY / DONE flags between
- * the ranks order it, every wait bounded by the library's wait limit (a
- * timeout is reported by zlift_device_error).  Up to 8 ranks.  0 success,
- * 1 bad arguments, 13 a CUDA call failed, 100 + ncclResult_t. */
+ * it with its own C, the same `bytes`, before the first step that uses it;
+ * the buffer ends up registered on every rank or on none (the ranks agree on
+ * the first nonzero status).  Afterwards zlift_part_gemm_ex_nsplit_overlap on
+ * this C gathers each sub-block straight into the peers' C instead of
+ * through ncclAllGather: by copy-engine copies, one stream per peer
+ * (default), or by a store kernel next to the GEMM of the following
+ * sub-block (ZLIFT_PART_GATHER=sm).  READY / DONE flags between the ranks
+ * order it, every wait bounded by the library's wait limit (a timeout is
+ * reported by zlift_device_error; a rank whose call failed part-way sends no
+ * DONE, so its peers time out rather than read partial columns).  Up to 8
+ * ranks.  Each exchange step waits at most 120 s for the other ranks, then
+ * aborts the communicator (200).  0 success, 1 bad arguments, 13 a CUDA call
+ * failed, 100 + ncclResult_t, 200 a rank did not arrive. */
 ZLIFT_API int zlift_part_register_peer_buffer(void *comm, int nranks, int rank, void *C,
                                              size_t bytes);
 /* Unmaps a registered C (after every rank's last use of it; waits for the

@@ -162,6 +162,8 @@ void release_overlap(void* comm) {
 // bounded by the library's wait limit and records kErrWaitTimeout.
 
 constexpr int kMaxRanks = 8;
+// deadline of each exchange step of zlift_part_register_peer_buffer
+constexpr int kRegisterTimeoutMs = 120000;
 enum { kReady = 0, kDone = 1 };
 
 struct PeerPtrs {
@@ -502,18 +504,27 @@ int zlift_part_register_peer_buffer(void* comm, int nranks, int rank, void* C, s
                                       cudaMemcpyHostToDevice) != cudaSuccess)) {
         rc = 13;
     }
-    // every rank takes part in the all-gather, even one that failed above (it
-    // sends zeros and then reports its error), so no rank waits for it
+    // Every rank takes part in both all-gathers, even one that failed above
+    // (it sends zeros, then its error code), so no rank waits for it.  Each
+    // gather is waited for with a deadline: a rank that never arrives aborts
+    // the communicator (200) instead of blocking here.
+    bool aborted = false;
+    auto gather = [&](const void* send, void* recv, size_t count) {
+        NcclResult r = nc.all_gather(send, recv, count, kNcclInt8, comm, st);
+        if (r != kNcclSuccess) {
+            if (rc == 0) rc = 100 + r;
+            return;
+        }
+        const int w = zlift_part_comm_wait(comm, st, kRegisterTimeoutMs);
+        if (w >= 100) aborted = true;
+        if (w && rc == 0) rc = w;
+    };
     if (dinfo && st) {
-        NcclResult r = nc.all_gather(dinfo + rank, dinfo, sizeof(Info), kNcclInt8, comm, st);
-        if (r != kNcclSuccess && rc == 0) rc = 100 + r;
-        if (cudaStreamSynchronize(st) != cudaSuccess && rc == 0) rc = 13;
-        if (cudaMemcpy(all.data(), dinfo, sizeof(Info) * nranks, cudaMemcpyDeviceToHost) !=
-                cudaSuccess && rc == 0)
+        gather(dinfo + rank, dinfo, sizeof(Info));
+        if (!aborted && cudaMemcpy(all.data(), dinfo, sizeof(Info) * nranks,
+                                   cudaMemcpyDeviceToHost) != cudaSuccess && rc == 0)
             rc = 13;
     }
-    if (st) cudaStreamDestroy(st);
-    if (dinfo) cudaFree(dinfo);
     for (int p = 0; rc == 0 && p < nranks; p++) {
         if (p == rank) {
             b.peer_C[p] = b.C;
@@ -534,6 +545,26 @@ int zlift_part_register_peer_buffer(void* comm, int nranks, int rank, void* C, s
         b.peer_flags[p] = static_cast<unsigned long long*>(pf);
         b.peer_C[p] = static_cast<char*>(pb) + all[p].off;
     }
+    // agreement: the buffer is registered on every rank or on none (each
+    // rank's status, gathered; the first nonzero one is every rank's result)
+    if (dinfo && st && !aborted) {
+        std::vector<int> codes(nranks, 0);
+        int* dcodes = reinterpret_cast<int*>(dinfo);
+        const int mine_rc = rc;
+        if (cudaMemcpy(dcodes + rank, &mine_rc, sizeof(int), cudaMemcpyHostToDevice) !=
+                cudaSuccess && rc == 0)
+            rc = 13;
+        gather(dcodes + rank, dcodes, sizeof(int));
+        if (!aborted && cudaMemcpy(codes.data(), dcodes, sizeof(int) * nranks,
+                                   cudaMemcpyDeviceToHost) == cudaSuccess) {
+            for (int p = 0; p < nranks && rc == 0; p++)
+                if (codes[p]) rc = codes[p];
+        } else if (rc == 0) {
+            rc = 13;
+        }
+    }
+    if (st) cudaStreamDestroy(st);
+    if (dinfo) cudaFree(dinfo);
     if (rc) {
         cudaGetLastError();
         close_peer_buf(b);
@@ -689,12 +720,16 @@ int zlift_part_gemm_ex_nsplit_overlap(void* handle, void* comm, int nranks, int 
                     rc = 13;
             }
         }
-        // tell every peer that all of its columns from this rank have landed
-        PeerPtrs done{};
-        for (int r = 0; r < nranks; r++)
-            if (r != rank) done.flag[r] = pbuf->peer_flags[r] + kDone * kMaxRanks + rank;
-        signal_peers_kernel<<<1, 32, 0, ov->stream>>>(done, nranks, epoch);
-        if (cudaGetLastError() != cudaSuccess && rc == 0) rc = 13;
+        // tell every peer that all of its columns from this rank have landed;
+        // a call that failed part-way does not, so its peers' bounded waits
+        // run out and report the failure instead of using partial columns
+        if (rc == 0) {
+            PeerPtrs done{};
+            for (int r = 0; r < nranks; r++)
+                if (r != rank) done.flag[r] = pbuf->peer_flags[r] + kDone * kMaxRanks + rank;
+            signal_peers_kernel<<<1, 32, 0, ov->stream>>>(done, nranks, epoch);
+            if (cudaGetLastError() != cudaSuccess) rc = 13;
+        }
         // the handle's stream continues once this rank's stores are out and
         // every peer's have arrived
         if (cudaEventRecord(ov->gathered, ov->stream) != cudaSuccess ||
