@@ -91,7 +91,12 @@ ZLIFT_API cublasStatus_t cublasLtMatmulAlgoGetHeuristic(void *lt, void *desc, vo
                                                         void *pref, int requested,
                                                         void *results, int *returned); /* :626 */
 /* D = epilogue(alpha * op(A) * op(B) + beta * C), column-major layouts,
- * batched when the layouts carry a batch count.  zblas.c:643-711. */
+ * batched when the layouts carry a batch count.  zblas.c:643-711.
+ * New (the reference has no int8 path): int8 A/B with compute 32I give an
+ * int32 D (int32 scalars, scale type CUDA_R_32I), or, with int8 C/D and
+ * scale type CUDA_R_32F, the requantised int8 D = saturate(round(alpha *
+ * acc + beta * C)) (float scalars, round to nearest even, [-128, 127]);
+ * int8 outputs take no bias/activation epilogue (NOT_SUPPORTED). */
 ZLIFT_API cublasStatus_t cublasLtMatmul(void *lt, void *desc, const void *alpha,
                                         const void *A, void *Adesc, const void *B, void *Bdesc,
                                         const void *beta, const void *C, void *Cdesc, void *D,

@@ -67,6 +67,9 @@ def oracle() -> ctypes.CDLL:
         lib.zo_gemm_entries.argtypes = [_int, _int, _int, _d, _vp, _int, _int, _vp, _int,
                                         _int, _d, _vp, _int, _int, _vp, _vp, _ll, _vp]
         lib.zo_dgemm.restype = None
+        lib.zo_gemm_i8_s8.restype = _int
+        lib.zo_gemm_i8_s8.argtypes = [_int, _int, _int, _int, _int, ctypes.c_float, _vp, _int,
+                                      _vp, _int, ctypes.c_float, _vp, _int]
         lib.zo_dgemm.argtypes = [_int, _int, _int, _int, _int, _d, _vp, _int, _vp, _int, _d,
                                  _vp, _int]
         lib.zo_lt_epilogue.restype = None
@@ -131,6 +134,13 @@ def gemm_strided_batched_ex(transa, transb, m, n, k, alpha, A, Atype, lda, sA, B
     return oracle().zo_gemm_strided_batched_ex(transa, transb, m, n, k, _p(al), _p(A), Atype,
                                                lda, sA, _p(B), Btype, ldb, sB, _p(be), _p(C),
                                                Ctype, ldc, sC, batch, compute)
+
+
+def gemm_i8_s8(transa, transb, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc) -> int:
+    """int8 C = sat_s8(rne(alpha * op(A) op(B) + beta * C)), float alpha/beta (in place)."""
+    assert A.dtype == np.int8 and B.dtype == np.int8 and C.dtype == np.int8
+    return oracle().zo_gemm_i8_s8(transa, transb, m, n, k, float(alpha), _p(A), lda, _p(B), ldb,
+                                  float(beta), _p(C), ldc)
 
 
 def dgemm(transa, transb, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc) -> None:

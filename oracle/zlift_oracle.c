@@ -22,6 +22,10 @@
  *       CUDA_R_32I, compute 32I) has no counterpart in the reference (which
  *       returns NOT_SUPPORTED, zblas/zblas.c:366-367); it is exact int32
  *       arithmetic with two's-complement wrap for alpha/beta scaling.
+ *   zo_gemm_i8_s8                         cublasLtMatmul's int8-output form
+ *       (int8 A/B/C/D, compute 32I, scale type 32F; not in the reference):
+ *       the exact int32 product, x = alpha * float(acc) (+ fmaf(beta,
+ *       float(C), x)), rounded to nearest even and saturated to int8.
  *   zo_dgemm                              cblas_dgemm as called at
  *       zblas/zblas.c:131-144 (fp64, summed in K order).
  *   zo_gemm_strided_batched_ex            zblas/zblas.c:491-511 (host loop
@@ -210,13 +214,28 @@ void zo_dgemm(int transa, int transb, int m, int n, int k, double alpha,
     }
 }
 
-/* int8 x int8 -> int32 with int32 alpha/beta; exact, wrapping.  Both
- * operands are packed K-contiguous, then 64 x 64 blocks of C are computed
- * from cache-resident rows. */
+/* int8 output with float scaling (cuBLASLt's int8 D with scale type 32F):
+ * x = alpha * float(acc), plus fmaf(beta, float(C), x) when beta != 0, then
+ * rounded to nearest with ties to even (lrintf in the default rounding
+ * mode) and saturated to [-128, 127]; NaN gives 0. */
+static int8_t requant_s8(int32_t acc, float alpha, float beta, int8_t old) {
+    float x = alpha * (float)acc;
+    if (beta != 0.0f) x = fmaf(beta, (float)old, x);
+    if (x != x) return 0;
+    if (x >= 127.0f) return 127;
+    if (x <= -128.0f) return -128;
+    return (int8_t)lrintf(x);
+}
+
+/* int8 x int8 products, exact with int32 wrap-around.  C8 == NULL: int32
+ * C = alpha * acc + beta * C with int32 alpha/beta (wrapping); otherwise
+ * the int8 C8 is requantised with the float fa/fb.  Both operands are packed
+ * K-contiguous, then 64 x 64 blocks of C are computed from cache-resident
+ * rows. */
 static void gemm_i8(int transa, int transb, int m, int n, int k,
                     int32_t alpha, const int8_t *A, int lda,
                     const int8_t *B, int ldb, int32_t beta,
-                    int32_t *C, int ldc) {
+                    int32_t *C, int ldc, int8_t *C8, float fa, float fb) {
     int8_t *pa = pack_i8(transa, A, m, k, lda, 0);
     int8_t *pb = pack_i8(transb, B, n, k, ldb, 1);
     if (!pa || !pb) { free(pa); free(pb); return; }
@@ -229,10 +248,16 @@ static void gemm_i8(int transa, int transb, int m, int n, int k,
         for (int j = j0; j < j1; j++) {
             const int8_t *bj = pb + (size_t)j * k;
             for (int i = i0; i < i1; i++) {
-                uint32_t r = (uint32_t)alpha * dot_i8(pa + (size_t)i * k, bj, k);
+                const uint32_t acc = dot_i8(pa + (size_t)i * k, bj, k);
+                const int64_t at = i + (int64_t)j * ldc;
+                if (C8) {
+                    C8[at] = requant_s8((int32_t)acc, fa, fb, C8[at]);
+                    continue;
+                }
+                uint32_t r = (uint32_t)alpha * acc;
                 if (beta != 0)
-                    r += (uint32_t)beta * (uint32_t)C[i + (int64_t)j * ldc];
-                C[i + (int64_t)j * ldc] = (int32_t)r;
+                    r += (uint32_t)beta * (uint32_t)C[at];
+                C[at] = (int32_t)r;
             }
         }
     }
@@ -315,7 +340,7 @@ int zo_gemm_ex(int transa, int transb, int m, int n, int k, const void *alpha,
         && (computeType == ZO_COMPUTE_32I || computeType == ZO_R_32I)) {
         gemm_i8(transa, transb, m, n, k, *(const int32_t *)alpha,
                 (const int8_t *)A, lda, (const int8_t *)B, ldb,
-                *(const int32_t *)beta, (int32_t *)C, ldc);
+                *(const int32_t *)beta, (int32_t *)C, ldc, NULL, 0.f, 0.f);
         return ZO_OK;
     }
     if (computeType != ZO_R_32F && computeType != ZO_COMPUTE_32F)
@@ -338,6 +363,16 @@ int zo_gemm_ex(int transa, int transb, int m, int n, int k, const void *alpha,
                          ldb, be, C, ct, ldc);
     }
     return ZO_NOT_SUPPORTED;
+}
+
+/* cublasLtMatmul with int8 A/B/C/D, compute 32I and scale type 32F (no
+ * counterpart in the reference): D = requant_s8(alpha * acc + beta * C),
+ * float alpha/beta. */
+int zo_gemm_i8_s8(int transa, int transb, int m, int n, int k, float alpha,
+                  const int8_t *A, int lda, const int8_t *B, int ldb, float beta,
+                  int8_t *C, int ldc) {
+    gemm_i8(transa, transb, m, n, k, 0, A, lda, B, ldb, 0, NULL, ldc, C, alpha, beta);
+    return ZO_OK;
 }
 
 static size_t zo_elem_size(int type) {

@@ -193,3 +193,133 @@ def test_lt_matmul_epilogues(built_lib, oracle_lib, cuda, kind, ta, tb, m, n, k,
         lib.cublasLtMatrixLayoutDestroy(l)
     lib.cublasLtMatmulDescDestroy(d)
     lib.cublasLtDestroy(h)
+
+
+# ---------------------------------------------------------------------------
+# int8 output (requantising epilogue): int8 A/B/C/D, compute 32I, scale 32F.
+# D = sat_s8(rne(alpha * float(acc) + beta * float(C))), bit-exact.
+
+def _requant_np(A, B, C0, ta, tb, m, n, k, alpha, beta):
+    """numpy restatement: exact int64 product, one float32 multiply, the
+    beta term added in float64 (exact for the power-of-two betas used here,
+    so it equals the single rounding of fmaf), ties to even, saturation."""
+    opA = (A.reshape(m, k, order="F") if ta == 0 else A.reshape(k, m, order="F").T).astype(np.int64)
+    opB = (B.reshape(k, n, order="F") if tb == 0 else B.reshape(n, k, order="F").T).astype(np.int64)
+    acc = (opA @ opB).astype(np.int32)
+    x = np.float32(alpha) * acc.astype(np.float32)
+    if beta != 0.0:
+        c = C0.reshape(m, n, order="F").astype(np.float64)
+        x = (np.float64(beta) * c + x.astype(np.float64)).astype(np.float32)
+    out = np.clip(np.rint(x), -128, 127).astype(np.int8)
+    return out.reshape(-1, order="F")
+
+
+@pytest.mark.parametrize("ta,tb,alpha,beta", [(1, 0, 0.5, 0.0), (0, 1, 0.013, 0.5),
+                                              (0, 0, 3.0, -0.25), (1, 1, 0.0071, 1.0)])
+def test_oracle_requant_matches_numpy(oracle_lib, ta, tb, alpha, beta):
+    """The oracle's int8-output GEMM: ties to even (alpha 0.5 makes every odd
+    accumulator a tie), saturation (alpha 3), and the beta term."""
+    from zlift_b200 import inputs
+    m, n, k = 37, 29, 70
+    A = inputs.make("i8", "int8", 91, m * k)
+    B = inputs.make("i8", "int8", 92, k * n)
+    C0 = inputs.make("i8", "int8", 93, m * n)
+    got = C0.copy()
+    assert oracle_lib.gemm_i8_s8(ta, tb, m, n, k, alpha, A, m if ta == 0 else k, B,
+                                 k if tb == 0 else n, beta, got, m) == 0
+    want = _requant_np(A, B, C0, ta, tb, m, n, k, alpha, beta)
+    np.testing.assert_array_equal(got, want)
+    if alpha == 3.0:
+        assert (got == 127).any() and (got == -128).any()
+
+
+I8_CASES = [
+    # (ta, tb, m, n, k, alpha, beta, ldc_pad, c_is_d): staged TMA epilogue,
+    # direct stores (ldc not a multiple of 16), the CUDA-core kernel (odd
+    # lda), a K-split shape (few tiles, long K), MN-major operands
+    (1, 0, 256, 384, 512, 0.01, 0.0, 0, True),
+    (1, 0, 512, 256, 1024, 0.003, 0.5, 0, False),
+    (1, 0, 200, 136, 256, 0.02, -0.25, 3, True),
+    (1, 0, 96, 80, 61, 0.05, 1.0, 0, True),
+    (1, 0, 128, 128, 8192, 0.0004, 0.5, 0, True),
+    (0, 1, 256, 256, 384, 0.01, 0.0, 0, True),
+    (0, 0, 256, 256, 256, 0.5, 0.0, 0, True),
+]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("ta,tb,m,n,k,alpha,beta,pad,c_is_d", I8_CASES)
+def test_lt_matmul_int8_out(built_lib, oracle_lib, cuda, ta, tb, m, n, k, alpha, beta, pad,
+                            c_is_d):
+    import torch
+    from zlift_b200 import inputs
+    lib = _lt(built_lib)
+    ar, ac = (m, k) if ta == 0 else (k, m)
+    br, bc = (k, n) if tb == 0 else (n, k)
+    ldc = m + pad
+    A = inputs.make("i8", "int8", 101, ar * ac)
+    B = inputs.make("i8", "int8", 102, br * bc)
+    C0 = inputs.make("i8", "int8", 103, ldc * n)
+    want = C0.copy()
+    assert oracle_lib.gemm_i8_s8(ta, tb, m, n, k, alpha, A, ar, B, br, beta, want, ldc) == 0
+    h = vp()
+    assert lib.cublasLtCreate(ctypes.byref(h)) == 0
+    d = vp()
+    assert lib.cublasLtMatmulDescCreate(ctypes.byref(d), 72, 0) == 0     # 32I compute, 32F scale
+    _set(lib, d, 3, ta)
+    _set(lib, d, 4, tb)
+    dA, dB = to_dev(A, "i8"), to_dev(B, "i8")
+    dC = to_dev(C0, "i8")
+    dD = dC if c_is_d else to_dev(np.zeros_like(C0), "i8")
+    la = _layout(lib, 3, ar, ac, ar)
+    lb = _layout(lib, 3, br, bc, br)
+    lc = _layout(lib, 3, m, n, ldc)
+    al, be = ctypes.c_float(alpha), ctypes.c_float(beta)
+    s = torch.cuda.current_stream().cuda_stream
+    st = lib.cublasLtMatmul(h, d, ctypes.byref(al), dA.data_ptr(), la, dB.data_ptr(), lb,
+                            ctypes.byref(be), dC.data_ptr(), lc, dD.data_ptr(), lc, None, None,
+                            0, s)
+    assert st == 0
+    torch.cuda.synchronize()
+    from zlift_b200 import blas
+    assert blas.device_error() == 0
+    got = from_dev(dD, "i8").reshape(n, ldc)
+    np.testing.assert_array_equal(got[:, :m], want.reshape(n, ldc)[:, :m])
+    if alpha >= 0.5:
+        assert (got[:, :m] == 127).any() or (got[:, :m] == -128).any()
+    if not c_is_d:
+        np.testing.assert_array_equal(from_dev(dC, "i8"), C0)
+    for l in (la, lb, lc):
+        lib.cublasLtMatrixLayoutDestroy(l)
+    lib.cublasLtMatmulDescDestroy(d)
+    lib.cublasLtDestroy(h)
+
+
+def test_lt_int8_out_rejections_on_host(built_lib):
+    """int8 D needs scale type 32F, takes no bias/activation epilogue, and
+    cublasGemmEx itself has no int8 output (NOT_SUPPORTED, as cuBLAS)."""
+    lib = _lt(built_lib)
+    h = vp()
+    assert lib.cublasLtCreate(ctypes.byref(h)) == 0
+    d = vp()
+    assert lib.cublasLtMatmulDescCreate(ctypes.byref(d), 72, 10) == 0    # scale type 32I
+    l = _layout(lib, 3, 16, 16, 16)
+    one = ctypes.c_float(1.0)
+    call = lambda: lib.cublasLtMatmul(h, d, ctypes.byref(one), 16, l, 16, l, ctypes.byref(one),
+                                      16, l, 16, l, None, None, 0, None)
+    assert call() == 15
+    _set(lib, d, 1, 0)                         # scale type 32F
+    _set(lib, d, 7, 2)                         # ReLU epilogue
+    assert call() == 15
+    hb = vp()
+    built_lib.cublasCreate_v2.argtypes = [ctypes.POINTER(vp)]
+    assert built_lib.cublasCreate_v2(ctypes.byref(hb)) == 0
+    built_lib.cublasGemmEx.argtypes = [vp, ci, ci, ci, ci, ci, vp, vp, ci, ci, vp, ci, ci, vp,
+                                       vp, ci, ci, ci, ci]
+    assert built_lib.cublasGemmEx(hb, 1, 0, 16, 16, 16, ctypes.byref(one), 16, 3, 16, 16, 3, 16,
+                                  ctypes.byref(one), 16, 3, 16, 72, 0) == 15
+    built_lib.cublasDestroy_v2.argtypes = [vp]
+    built_lib.cublasDestroy_v2(hb)
+    lib.cublasLtMatrixLayoutDestroy(l)
+    lib.cublasLtMatmulDescDestroy(d)
+    lib.cublasLtDestroy(h)

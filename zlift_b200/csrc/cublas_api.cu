@@ -248,6 +248,7 @@ struct LtExtra {
     int bias_type;
     cudaStream_t stream;
     int pointer_mode;
+    int scale_type;
 };
 
 // Type/compute dispatch of cublasGemmEx (zblas/zblas.c:357-391) for one
@@ -269,10 +270,15 @@ static cublasStatus_t gemm_ex(Handle* h, int transa, int transb, int m, int n, i
     d.B = B; d.ldb = ldb; d.strideB = sB; d.Btype = Btype;
     d.C = C; d.ldc = ldc; d.strideC = sC; d.Ctype = Ctype;
     bool integer = false;
-    if (Atype == kR8I && Btype == kR8I && Ctype == kR32I &&
-        (computeType == CUBLAS_COMPUTE_32I || computeType == kR32I)) {
+    const bool compute_i = computeType == CUBLAS_COMPUTE_32I || computeType == kR32I;
+    if (Atype == kR8I && Btype == kR8I && Ctype == kR32I && compute_i) {
         d.kind = Kind::I8;
         integer = true;
+    } else if (lt && Atype == kR8I && Btype == kR8I && Ctype == kR8I && compute_i) {
+        // cuBLASLt's int8 output: float alpha/beta (scale type 32F),
+        // D = sat_s8(rne(alpha * acc + beta * C)) -- the requantising epilogue
+        if (lt->scale_type != kR32F) return CUBLAS_STATUS_NOT_SUPPORTED;
+        d.kind = Kind::I8;
     } else {
         if (computeType != kR32F && computeType != CUBLAS_COMPUTE_32F)
             return CUBLAS_STATUS_NOT_SUPPORTED;
@@ -286,7 +292,7 @@ static cublasStatus_t gemm_ex(Handle* h, int transa, int transb, int m, int n, i
             return CUBLAS_STATUS_NOT_SUPPORTED;
         }
     }
-    if (lt && lt->epi && integer) return CUBLAS_STATUS_NOT_SUPPORTED;
+    if (lt && lt->epi && d.kind == Kind::I8) return CUBLAS_STATUS_NOT_SUPPORTED;
     if (m == 0 || n == 0 || batch == 0) return CUBLAS_STATUS_SUCCESS;
     if (!C || (k > 0 && (!A || !B))) return CUBLAS_STATUS_INVALID_VALUE;
     st = set_scalars(lt ? lt->pointer_mode : h->pointer_mode, d, alpha, beta, integer);
@@ -745,6 +751,7 @@ cublasStatus_t cublasLtMatmul(void* lt, void* desc, const void* alpha, const voi
     x.bias_type = (ld_->type == kR16F || ld_->type == kR16BF) ? ld_->type : kR32F;
     x.stream = static_cast<cudaStream_t>(stream);
     x.pointer_mode = d->pointer_mode;
+    x.scale_type = d->scale_type;
     // C != D: D starts as a copy of C (zblas.c:681-686), on the call's stream
     if (C && C != D && m > 0 && n > 0) {
         const size_t es = elem_size(ld_->type);

@@ -67,6 +67,20 @@ struct GemmDesc {
 
 enum EpiFlags : int { kEpiBias = 1, kEpiRelu = 2, kEpiGelu = 4 };
 
+// int8 output of an int32 accumulator with float scaling (cuBLASLt's int8 D
+// with a 32F scale type): x = alpha * float(acc) (+ beta * float(C)), then
+// rounded to nearest with ties to even and saturated to [-128, 127]; NaN
+// gives 0.  The float steps are explicit (one rounded multiply, one fused
+// multiply-add) so that a CPU restatement reproduces every bit.
+__device__ __forceinline__ int8_t requant_s8(int32_t acc, float alpha, bool use_beta, float beta,
+                                             int8_t old) {
+    float x = __fmul_rn(alpha, __int2float_rn(acc));
+    if (use_beta) x = __fmaf_rn(beta, __int2float_rn((int)old), x);
+    if (x != x) return 0;
+    const int r = __float2int_rn(x);
+    return (int8_t)(r < -128 ? -128 : (r > 127 ? 127 : r));
+}
+
 // x after the fused epilogue (bias already added by the caller if requested)
 __host__ __device__ inline float apply_act(float x, int epi) {
     if (epi & kEpiRelu) x = x > 0.f ? x : 0.f;

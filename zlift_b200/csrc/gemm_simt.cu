@@ -96,12 +96,15 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(const SimtParams p) {
     }
     float alpha = p.alpha, beta = p.beta;
     int32_t ia = p.ia, ib = p.ib;
+    // int32 scalars for int32 C; float for every other output (int8 C is
+    // requantised with float scaling)
+    const bool iscale = INT && p.Ct == kR32I;
     if (p.alpha_dev) {
-        if constexpr (INT) ia = *static_cast<const int32_t*>(p.alpha_dev);
+        if (iscale) ia = *static_cast<const int32_t*>(p.alpha_dev);
         else alpha = *static_cast<const float*>(p.alpha_dev);
     }
     if (p.beta_dev) {
-        if constexpr (INT) ib = *static_cast<const int32_t*>(p.beta_dev);
+        if (iscale) ib = *static_cast<const int32_t*>(p.beta_dev);
         else beta = *static_cast<const float*>(p.beta_dev);
     }
     const long long gi = i0 + tx;
@@ -113,10 +116,15 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(const SimtParams p) {
         if (gj >= p.n) continue;
         const long long at = (long long)bz * p.sC + gi + gj * p.ldc;
         if constexpr (INT) {
-            int32_t* cp = static_cast<int32_t*>(p.C) + at;
-            uint32_t v = (uint32_t)ia * (uint32_t)iacc[c];
-            if (ib != 0) v += (uint32_t)ib * (uint32_t)(*cp);
-            *cp = (int32_t)v;
+            if (p.Ct == kR8I) {
+                int8_t* cp = static_cast<int8_t*>(p.C) + at;
+                *cp = requant_s8(iacc[c], alpha, beta != 0.f, beta, beta != 0.f ? *cp : 0);
+            } else {
+                int32_t* cp = static_cast<int32_t*>(p.C) + at;
+                uint32_t v = (uint32_t)ia * (uint32_t)iacc[c];
+                if (ib != 0) v += (uint32_t)ib * (uint32_t)(*cp);
+                *cp = (int32_t)v;
+            }
         } else {
             float v = alpha * acc[c];
             if (p.Ct == kR16F) {

@@ -54,6 +54,13 @@ template <> struct KT<(int)Kind::TF32X3> { static constexpr int es = 4, uk = 8, 
 template <> struct KT<(int)Kind::TF32>   { static constexpr int es = 4, uk = 8,  cfmt = 1, abfmt = 2, planes = 1; };
 template <> struct KT<(int)Kind::I8>     { static constexpr int es = 1, uk = 32, cfmt = 2, abfmt = 1, planes = 1; };
 
+// bytes of one output element
+__host__ __device__ constexpr int out_es(int out) {
+    return out == kR8I ? 1 : (out == kR16F || out == kR16BF) ? 2 : 4;
+}
+// outputs computed from an int32 accumulator (int32 C, or int8 C requantised)
+__host__ __device__ constexpr bool int_acc(int out) { return out == kR32I || out == kR8I; }
+
 struct TcParams {
     int m, n, k, batch;
     int tiles_m, tiles_n, k_blocks;
@@ -161,7 +168,7 @@ __device__ __forceinline__ void combine_parts(uint32_t (&v)[32], const uint32_t*
             }
 #pragma unroll
             for (int j = 0; j < 16; j++) {
-                if constexpr (OUT == kR32I) acc[j] = q ? acc[j] + x[j] : x[j];
+                if constexpr (int_acc(OUT)) acc[j] = q ? acc[j] + x[j] : x[j];
                 else acc[j] = q ? __float_as_uint(__uint_as_float(acc[j]) + __uint_as_float(x[j])) : x[j];
             }
         }
@@ -218,7 +225,6 @@ __device__ __forceinline__ float load_bias(const TcParams& p, long long row) {
     }
 }
 
-__host__ __device__ constexpr int out_es(int out) { return (out == kR16F || out == kR16BF) ? 2 : 4; }
 
 // Epilogue staging: two buffers of 32 output columns x 128 rows, laid out
 // [column][row] (rows contiguous, as in column-major C), moved to and from
@@ -322,7 +328,9 @@ __device__ __forceinline__ uint64_t operand_desc(uint32_t base, int ks) {
 // Raw bits of C's old value (for beta * C), read ahead of the stores.
 template <int OUT>
 __device__ __forceinline__ uint32_t load_c(const void* C, long long at) {
-    if constexpr (OUT == kR16F || OUT == kR16BF)
+    if constexpr (OUT == kR8I)
+        return static_cast<const uint8_t*>(C)[at];
+    else if constexpr (OUT == kR16F || OUT == kR16BF)
         return static_cast<const uint16_t*>(C)[at];
     else
         return static_cast<const uint32_t*>(C)[at];
@@ -337,6 +345,9 @@ __device__ __forceinline__ void store_out(void* C, long long at, uint32_t raw, u
         uint32_t v = (uint32_t)ia * raw;                 // two's-complement wrap
         if (use_beta) v += (uint32_t)ib * old;
         static_cast<int32_t*>(C)[at] = (int32_t)v;
+    } else if constexpr (OUT == kR8I) {
+        static_cast<int8_t*>(C)[at] =
+            requant_s8((int32_t)raw, alpha, use_beta, beta, (int8_t)(uint8_t)old);
     } else {
         float v = alpha * __uint_as_float(raw);
         if constexpr (OUT == kR32F) {
@@ -374,6 +385,9 @@ __device__ __forceinline__ void convert_chunk_t(const uint32_t (&v)[32], uint8_t
             uint32_t x = (uint32_t)ia * v[j];
             if constexpr (BETA) x += (uint32_t)ib * *reinterpret_cast<uint32_t*>(e);
             *reinterpret_cast<uint32_t*>(e) = x;
+        } else if constexpr (OUT == kR8I) {
+            *reinterpret_cast<int8_t*>(e) =
+                requant_s8((int32_t)v[j], alpha, BETA, beta, BETA ? *reinterpret_cast<int8_t*>(e) : 0);
         } else {
             float x = alpha * __uint_as_float(v[j]);
             if constexpr (OUT == kR32F) {
@@ -398,7 +412,7 @@ template <int OUT>
 __device__ __forceinline__ void convert_chunk(const uint32_t (&v)[32], uint8_t* sbuf, int row,
                                               float alpha, float beta, int32_t ia, int32_t ib,
                                               bool use_beta, int epi, float bias_row) {
-    if constexpr (OUT == kR32I) {
+    if constexpr (int_acc(OUT)) {
         if (use_beta) convert_chunk_t<OUT, true, false>(v, sbuf, row, alpha, beta, ia, ib, 0, 0.f);
         else convert_chunk_t<OUT, false, false>(v, sbuf, row, alpha, beta, ia, ib, 0, 0.f);
     } else if (epi) {
@@ -1076,6 +1090,7 @@ bool make_cmap(CUtensorMap* tm, const GemmDesc& d) {
     case kR16BF: t = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16; es = 2; break;
     case kR32F: t = CU_TENSOR_MAP_DATA_TYPE_FLOAT32; es = 4; break;
     case kR32I: t = CU_TENSOR_MAP_DATA_TYPE_INT32; es = 4; break;
+    case kR8I: t = CU_TENSOR_MAP_DATA_TYPE_UINT8; es = 1; break;
     default: return false;
     }
     if ((reinterpret_cast<uintptr_t>(d.C) & 15u) || (d.ldc * es) % 16) return false;
@@ -1256,6 +1271,7 @@ template <int KIND, int BN>
 int launch_major(const GemmDesc& d, bool a_mn, bool b_mn, const Maps& m, const TcParams& p,
                  cudaStream_t s) {
     if constexpr (KIND == (int)Kind::I8) {
+        if (d.Ctype == kR8I) return launch_majors<KIND, BN, kR8I>(a_mn, b_mn, m, p, s);
         if (d.Ctype != kR32I) return 1;
         return launch_majors<KIND, BN, kR32I>(a_mn, b_mn, m, p, s);
     } else if constexpr (KIND == (int)Kind::TF32X3 || KIND == (int)Kind::TF32) {
@@ -1383,7 +1399,7 @@ int gemm_tc(const GemmDesc& d, cudaStream_t s) {
     p.alpha = d.alpha; p.beta = d.beta;
     p.ialpha = d.ialpha; p.ibeta = d.ibeta;
     p.alpha_dev = d.alpha_dev; p.beta_dev = d.beta_dev;
-    p.epi = d.Ctype == kR32I ? 0 : d.epi;
+    p.epi = d.kind == Kind::I8 ? 0 : d.epi;
     p.bias = d.bias;
     p.bias_type = d.bias_type;
     p.work = d.split_work;
