@@ -37,7 +37,10 @@ on the launching stream and reduced with MAX over ranks; the region is
 repeated (`repeats`) so that the clock sampler sees the GPU under load for
 a while, and the median repeat is reported.  `e2e` repeats the step
 through the same C ABI with pinned host buffers copied in and the result
-copied out inside the timed region.  `cpu_baseline` (rank 0, N=1) and
+copied out inside the timed region, every step: pipelined over two device
+buffer slots (step i+1's upload on one copy stream while step i computes
+and downloads on another; PCIe is full duplex), with the one-stream serial
+figure reported beside it (`serial_ms_per_step`).  `cpu_baseline` (rank 0, N=1) and
 `--impl reference` time the reference's own CPU implementation -- zblas.c
 built from the reference sources (oracle/_ref) where the reference has a
 CPU path, the oracle's C restatement where it has none (int8, attention) --
@@ -193,6 +196,17 @@ class Workload:
     def config(self):
         return self.config_for(self.world)
 
+    # e2e: two device buffer slots; step i uploads slot i % 2's inputs from
+    # pinned host memory, runs the step on them and downloads its result
+    def e2e_upload(self, slot):
+        raise NotImplementedError
+
+    def e2e_compute(self, slot):
+        raise NotImplementedError
+
+    def e2e_download(self, slot):
+        raise NotImplementedError
+
     def close(self):
         pass
 
@@ -226,7 +240,7 @@ class GemmF16(Workload):
         self.kernel_bytes = 2.0 * (M * K + K * N + 2 * M * N)
         A, B, C = self.sets[0]
         self.hA, self.hB, self.hC = (t.cpu().pin_memory() for t in (A, B, C))
-        self.hOut = torch.empty_like(self.hC).pin_memory()
+        self.hOut = [torch.empty_like(self.hC).pin_memory() for _ in range(2)]
 
     def step(self, i):
         A, B, C = self.sets[i % 3]
@@ -234,13 +248,15 @@ class GemmF16(Workload):
                             0.5, C, 2, self.M)
         assert st == 0, st
 
-    def e2e_step(self):
-        A, B, C = self.sets[0]
-        A.copy_(self.hA, non_blocking=True)
-        B.copy_(self.hB, non_blocking=True)
-        C.copy_(self.hC, non_blocking=True)
-        self.step(0)
-        self.hOut.copy_(C, non_blocking=True)
+    def e2e_upload(self, slot):
+        for d, hsrc in zip(self.sets[slot], (self.hA, self.hB, self.hC)):
+            d.copy_(hsrc, non_blocking=True)
+
+    def e2e_compute(self, slot):
+        self.step(slot)
+
+    def e2e_download(self, slot):
+        self.hOut[slot].copy_(self.sets[slot][2], non_blocking=True)
 
     def e2e_bytes(self):
         return 2 * (2 * self.M * self.K + self.M * self.N), 2 * self.M * self.N
@@ -287,27 +303,38 @@ class GemmBF16Batched(Workload):
         self.A = _gen("bf16", (self.BATCH, K, M), 40, dev)
         self.B = _gen("bf16", (self.BATCH, N, K), 50, dev)
         self.C = torch.empty(self.BATCH, N, M, dtype=torch.bfloat16, device=dev)
+        # the e2e pipeline's second buffer slot
+        self.slots = [(self.A, self.B, self.C),
+                      tuple(torch.empty_like(t) for t in (self.A, self.B, self.C))]
         nb = hi - lo
         self.flops = 2.0 * M * N * K * self.BATCH
         self.kernel_flops = 2.0 * M * N * K * nb
         self.kernel_bytes = 2.0 * (M * K + K * N + M * N) * nb
         self.hA = self.A[lo:hi].cpu().pin_memory()
         self.hB = self.B[lo:hi].cpu().pin_memory()
-        self.hC = torch.empty_like(self.C[lo:hi], device="cpu").pin_memory()
+        self.hC = [torch.empty_like(self.C[lo:hi], device="cpu").pin_memory() for _ in range(2)]
 
-    def step(self, i):
+    def _gemm(self, A, B, C):
         from zlift_b200 import partition
         M, N, K = self.M, self.N, self.K
         st = partition.gemm_strided_batched_range(
-            self.h, self.lo, self.hi, 0, 0, M, N, K, 1.0 / math.sqrt(K), self.A, 14, M, M * K,
-            self.B, 14, K, K * N, 0.0, self.C, 14, M, M * N, 68)
+            self.h, self.lo, self.hi, 0, 0, M, N, K, 1.0 / math.sqrt(K), A, 14, M, M * K,
+            B, 14, K, K * N, 0.0, C, 14, M, M * N, 68)
         assert st == 0, st
 
-    def e2e_step(self):
-        self.A[self.lo:self.hi].copy_(self.hA, non_blocking=True)
-        self.B[self.lo:self.hi].copy_(self.hB, non_blocking=True)
-        self.step(0)
-        self.hC.copy_(self.C[self.lo:self.hi], non_blocking=True)
+    def step(self, i):
+        self._gemm(self.A, self.B, self.C)
+
+    def e2e_upload(self, slot):
+        A, B, _ = self.slots[slot]
+        A[self.lo:self.hi].copy_(self.hA, non_blocking=True)
+        B[self.lo:self.hi].copy_(self.hB, non_blocking=True)
+
+    def e2e_compute(self, slot):
+        self._gemm(*self.slots[slot])
+
+    def e2e_download(self, slot):
+        self.hC[slot].copy_(self.slots[slot][2][self.lo:self.hi], non_blocking=True)
 
     def e2e_bytes(self):
         nb = self.hi - self.lo
@@ -372,6 +399,9 @@ class GemmI8(Workload):
         self.A = _gen("i8", (self.M, self.K), 60, dev)                 # stored K x M (op T)
         self.B = _gen("i8", (self.nl, self.K), 70 + rank, dev)          # K x nl column block
         self.C = torch.empty(self.N, self.M, dtype=torch.int32, device=dev)   # full m x n
+        # the e2e pipeline's second buffer slot
+        self.slots = [(self.A, self.B, self.C),
+                      tuple(torch.empty_like(t) for t in (self.A, self.B, self.C))]
         self.comm = None
         if world > 1 and self.gather:
             box = [partition.Comm.unique_id() if rank == 0 else None]
@@ -379,42 +409,52 @@ class GemmI8(Workload):
             self.comm = partition.Comm(world, rank, box[0])
             if self.overlap:
                 # the overlapped gather stores into the peers' C directly
-                rc = self.comm.register_peer_buffer(self.C, self.C.numel() * 4)
-                assert rc == 0, rc
+                for _, _, C in self.slots:
+                    rc = self.comm.register_peer_buffer(C, C.numel() * 4)
+                    assert rc == 0, rc
         self.flops = 2.0 * self.M * self.N * self.K
         self.kernel_flops = 2.0 * self.M * self.nl * self.K
         self.kernel_bytes = float(self.M * self.K + self.K * self.nl + 4 * self.M * self.nl)
         if world > 1 and self.gather:
             self.launches_per_step = 1     # plus NCCL's own kernel
         self.hA, self.hB = self.A.cpu().pin_memory(), self.B.cpu().pin_memory()
-        self.hC = torch.empty(self.N * self.M, dtype=torch.int32).pin_memory()
+        self.hC = [torch.empty(self.N * self.M, dtype=torch.int32).pin_memory()
+                   for _ in range(2)]
 
-    def step(self, i):
+    def _gemm(self, A, B, C):
         from zlift_b200 import partition
         if self.gather and self.overlap and self.world > 1:
             st = partition.gemm_ex_nsplit_overlap(
                 self.h, self.comm, self.world, self.rank, sub_blocks_for(self.N, self.world), 1,
-                0, self.M, self.N, self.K, 1, self.A, 3, self.K, self.B, 3, self.K, 0, self.C,
-                10, 72)
+                0, self.M, self.N, self.K, 1, A, 3, self.K, B, 3, self.K, 0, C, 10, 72)
         elif self.gather:
             st = partition.gemm_ex_nsplit(self.h, self.comm, self.world, self.rank, 1, 0, self.M,
-                                          self.N, self.K, 1, self.A, 3, self.K, self.B, 3,
-                                          self.K, 0, self.C, 10, 72)
+                                          self.N, self.K, 1, A, 3, self.K, B, 3, self.K, 0, C,
+                                          10, 72)
         else:
-            cblk = self.C[self.n0:self.n0 + self.nl]
-            st = self.h.gemm_ex(1, 0, self.M, self.nl, self.K, 1, self.A, 3, self.K, self.B, 3,
-                                self.K, 0, cblk, 10, self.M, compute=72)
+            cblk = C[self.n0:self.n0 + self.nl]
+            st = self.h.gemm_ex(1, 0, self.M, self.nl, self.K, 1, A, 3, self.K, B, 3, self.K, 0,
+                                cblk, 10, self.M, compute=72)
         assert st == 0, st
 
-    def e2e_step(self):
-        self.A.copy_(self.hA, non_blocking=True)
-        self.B.copy_(self.hB, non_blocking=True)
-        self.step(0)
+    def step(self, i):
+        self._gemm(self.A, self.B, self.C)
+
+    def e2e_upload(self, slot):
+        A, B, _ = self.slots[slot]
+        A.copy_(self.hA, non_blocking=True)
+        B.copy_(self.hB, non_blocking=True)
+
+    def e2e_compute(self, slot):
+        self._gemm(*self.slots[slot])
+
+    def e2e_download(self, slot):
+        C = self.slots[slot][2]
         if self.gather:
-            self.hC.copy_(self.C.view(-1), non_blocking=True)
+            self.hC[slot].copy_(C.view(-1), non_blocking=True)
         else:
-            self.hC[:self.nl * self.M].copy_(self.C[self.n0:self.n0 + self.nl].reshape(-1),
-                                              non_blocking=True)
+            self.hC[slot][:self.nl * self.M].copy_(C[self.n0:self.n0 + self.nl].reshape(-1),
+                                                    non_blocking=True)
 
     def e2e_bytes(self):
         out = 4 * self.N * self.M if self.gather else 4 * self.nl * self.M
@@ -483,23 +523,36 @@ class Fmha(Workload):
         self.kernel_flops = full * (hi - lo)
         self.kernel_bytes = (hi - lo) * (4 * 2 * self.S * self.D + 4 * self.S)
         self.hq, self.hk, self.hv = (t.cpu().pin_memory() for t in (self.q, self.k, self.v))
-        self.ho = torch.empty_like(self.o, device="cpu").pin_memory()
+        self.ho = [torch.empty_like(self.o, device="cpu").pin_memory() for _ in range(2)]
         from zlift_b200 import attention
         self.blk = attention.flash_block(self.q, self.k, self.v, self.o, self.lse, causal=True)
+        # the e2e pipeline's second buffer slot
+        q2, k2, v2, o2, l2 = (torch.empty_like(t) for t in (self.q, self.k, self.v, self.o,
+                                                            self.lse))
+        self.slots = [(self.q, self.k, self.v, self.o, self.blk),
+                      (q2, k2, v2, o2, attention.flash_block(q2, k2, v2, o2, l2, causal=True))]
+        self._lse2 = l2
 
-    def step(self, i):
+    def _run(self, blk):
         from zlift_b200 import partition
         if self.hi <= self.lo:
             return
-        rc = partition.flash_pairs(self.blk, 1, self.lo - self.b0 * self.H,
+        rc = partition.flash_pairs(blk, 1, self.lo - self.b0 * self.H,
                                    self.hi - self.b0 * self.H, self.stream)
         assert rc == 0, rc
 
-    def e2e_step(self):
-        for d, hsrc in ((self.q, self.hq), (self.k, self.hk), (self.v, self.hv)):
+    def step(self, i):
+        self._run(self.blk)
+
+    def e2e_upload(self, slot):
+        for d, hsrc in zip(self.slots[slot][:3], (self.hq, self.hk, self.hv)):
             d.copy_(hsrc, non_blocking=True)
-        self.step(0)
-        self.ho.copy_(self.o, non_blocking=True)
+
+    def e2e_compute(self, slot):
+        self._run(self.slots[slot][4])
+
+    def e2e_download(self, slot):
+        self.ho[slot].copy_(self.slots[slot][3], non_blocking=True)
 
     def e2e_bytes(self):
         n = self.q.numel() * 2
@@ -545,19 +598,23 @@ class Sgemm(Workload):
         self.kernel_bytes = 3 * 4 * M * M
         self.launches_per_step = 3   # two tf32 split kernels + the GEMM
         self.hA, self.hB = self.sets[0][0].cpu().pin_memory(), self.sets[0][1].cpu().pin_memory()
-        self.hC = torch.empty(M, M).pin_memory()
+        self.hC = [torch.empty(M, M).pin_memory() for _ in range(2)]
 
     def step(self, i):
         A, B, C = self.sets[i % len(self.sets)]
         st = self.h.sgemm(0, 0, self.M, self.N, self.K, 1.0, A, self.M, B, self.K, 0.0, C, self.M)
         assert st == 0, st
 
-    def e2e_step(self):
-        A, B, C = self.sets[0]
+    def e2e_upload(self, slot):
+        A, B, _ = self.sets[slot]
         A.copy_(self.hA, non_blocking=True)
         B.copy_(self.hB, non_blocking=True)
-        self.step(0)
-        self.hC.copy_(C, non_blocking=True)
+
+    def e2e_compute(self, slot):
+        self.step(slot)
+
+    def e2e_download(self, slot):
+        self.hC[slot].copy_(self.sets[slot][2], non_blocking=True)
 
     def e2e_bytes(self):
         return 8 * self.M * self.M, 4 * self.M * self.M
@@ -770,22 +827,67 @@ def run_workload(W, h, dev, rank, world, local, stream, steps, warmup, clk, pk, 
     kernel_ms = statistics.mean(per_step)
 
     # ---- e2e through the same C ABI with host buffers ----
-    e2e_steps = max(3, min(20, steps))
-    with torch.cuda.stream(stream):
-        w.e2e_step()
-    torch.cuda.synchronize()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    barrier()
-    torch.cuda.synchronize()
-    with torch.cuda.stream(stream):
+    # Every step uploads its inputs from pinned host memory, runs, and
+    # downloads its result.  Pipelined (the reported figure): two device
+    # buffer slots, uploads on one copy stream and downloads on another, so
+    # step i+1's upload runs while step i computes and downloads (PCIe is
+    # full duplex); a slot is re-uploaded only after its previous result has
+    # been downloaded.  Serial (reported beside it): one slot, each step's
+    # upload, kernel and download in order on one stream.
+    e2e_steps = max(4, min(20, steps))
+    s_in = torch.cuda.Stream(device=dev)
+    s_out = torch.cuda.Stream(device=dev)
+
+    def e2e_pipelined(n):
+        up = [torch.cuda.Event() for _ in range(2)]
+        done = [torch.cuda.Event() for _ in range(2)]
+        down = [torch.cuda.Event() for _ in range(2)]
+        begin = torch.cuda.Event()
+        begin.record(stream)
+        s_in.wait_event(begin)
+        s_out.wait_event(begin)
+        for i in range(n):
+            slot = i % 2
+            if i >= 2:
+                s_in.wait_event(down[slot])
+            with torch.cuda.stream(s_in):
+                w.e2e_upload(slot)
+            up[slot].record(s_in)
+            stream.wait_event(up[slot])
+            with torch.cuda.stream(stream):
+                w.e2e_compute(slot)
+            done[slot].record(stream)
+            s_out.wait_event(done[slot])
+            with torch.cuda.stream(s_out):
+                w.e2e_download(slot)
+            down[slot].record(s_out)
+        for slot in range(min(n, 2)):
+            stream.wait_event(down[slot])
+
+    def e2e_serial(n):
+        with torch.cuda.stream(stream):
+            for _ in range(n):
+                w.e2e_upload(0)
+                w.e2e_compute(0)
+                w.e2e_download(0)
+
+    def e2e_time(fn):
+        fn(2)                                   # warm both slots and streams
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        barrier()
+        torch.cuda.synchronize()
         e0.record(stream)
-        for _ in range(e2e_steps):
-            w.e2e_step()
+        fn(e2e_steps)
         e1.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps)
-    barrier()
+        torch.cuda.synchronize()
+        ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps)
+        barrier()
+        return ms
+
+    e2e_ms = e2e_time(e2e_pipelined)
+    e2e_serial_ms = e2e_time(e2e_serial)
     bi, bo = w.e2e_bytes()
 
     rec = None
@@ -833,7 +935,13 @@ def run_workload(W, h, dev, rank, world, local, stream, steps, warmup, clk, pk, 
                                       if (w.name.startswith("gemm_i8") and w.gather and world > 1)
                                       else "")},
             "e2e": {"value": w.flops / (e2e_ms * 1e-3) / 1e12, "unit": w.unit,
-                    "h2d_bytes_per_step": bi, "d2h_bytes_per_step": bo, "ms_per_step": e2e_ms},
+                    "h2d_bytes_per_step": bi, "d2h_bytes_per_step": bo, "ms_per_step": e2e_ms,
+                    "steps": e2e_steps,
+                    "timing": "pipelined over 2 buffer slots: upload (copy stream) -> kernel "
+                              "-> download (second copy stream); every step copies its own "
+                              "inputs and result",
+                    "serial_ms_per_step": e2e_serial_ms,
+                    "serial_value": w.flops / (e2e_serial_ms * 1e-3) / 1e12},
             "gpu_launches": int(launches),
             "clocks": clocks,
         }
