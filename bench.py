@@ -797,11 +797,9 @@ def run_workload(W, h, dev, rank, world, local, stream, steps, warmup, clk, pk, 
     reps = int(max_over_ranks(reps))
 
     launches0 = blas.launch_count()
-    rep_ms, per_step = [], []
+    rep_ms = []
     windows = []
     for r in range(reps):
-        starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
-        ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
         t_start = torch.cuda.Event(enable_timing=True)
         t_end = torch.cuda.Event(enable_timing=True)
         barrier()
@@ -810,21 +808,49 @@ def run_workload(W, h, dev, rank, world, local, stream, steps, warmup, clk, pk, 
         with torch.cuda.stream(stream):
             t_start.record(stream)
             for i in range(steps):
-                starts[i].record(stream)
                 w.step(i)
-                ends[i].record(stream)
             t_end.record(stream)
         torch.cuda.synchronize()
         windows.append((w0, time.perf_counter()))
         barrier()
         rep_ms.append(max_over_ranks(t_start.elapsed_time(t_end)))
-        per_step.extend(s.elapsed_time(e) for s, e in zip(starts, ends))
     launches = (blas.launch_count() - launches0) // reps
     assert blas.device_error() == 0
     ms_total = statistics.median(rep_ms)
     ms_per_step = ms_total / steps
     value = w.flops / (ms_per_step * 1e-3) / 1e12
-    kernel_ms = statistics.mean(per_step)
+
+    # Per-call durations, in a separate pass: an event recorded between two
+    # calls makes the stream finish the first before it starts the second,
+    # which exposes the launch latency the back-to-back region above hides
+    # (up to ~15 us per call for the batched GEMM), so the timed region
+    # carries no per-step events.
+    per_step = []
+    for r in range(min(reps, 5)):
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+        barrier()
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            for i in range(steps):
+                starts[i].record(stream)
+                w.step(i)
+                ends[i].record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        per_step.extend(a.elapsed_time(b) for a, b in zip(starts, ends))
+    per_call_ms = statistics.mean(per_step)
+    if w.launches_per_step == 1 and world == 1:
+        # one launch of the dominant kernel per step: its average duration is
+        # the back-to-back region's time per step (an upper bound: it also
+        # holds the gaps between launches)
+        kernel_ms = ms_per_step
+        kernel_how = "timed region (CUDA events at its ends) / steps, one launch per step"
+    else:
+        kernel_ms = per_call_ms
+        kernel_how = "per-step CUDA events around each call" + (
+            " (GEMM + NCCL all-gather)"
+            if (w.name.startswith("gemm_i8") and w.gather and world > 1) else "")
 
     # ---- e2e through the same C ABI with host buffers ----
     # Every step uploads its inputs from pinned host memory, runs, and
@@ -930,10 +956,8 @@ def run_workload(W, h, dev, rank, world, local, stream, steps, warmup, clk, pk, 
                                            "per output term; frac per useful fp32 FLOP)"),
                          "traffic": traffic_from_profile(w.name) if world == 1 else None,
                          "kernel_ms": kernel_ms,
-                         "kernel": "per-step CUDA events around each call"
-                                   + (" (GEMM + NCCL all-gather)"
-                                      if (w.name.startswith("gemm_i8") and w.gather and world > 1)
-                                      else "")},
+                         "kernel": kernel_how,
+                         "per_call_events_ms": per_call_ms},
             "e2e": {"value": w.flops / (e2e_ms * 1e-3) / 1e12, "unit": w.unit,
                     "h2d_bytes_per_step": bi, "d2h_bytes_per_step": bo, "ms_per_step": e2e_ms,
                     "steps": e2e_steps,
