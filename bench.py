@@ -840,12 +840,14 @@ def run_workload(W, h, dev, rank, world, local, stream, steps, warmup, clk, pk, 
         barrier()
         per_step.extend(a.elapsed_time(b) for a, b in zip(starts, ends))
     per_call_ms = statistics.mean(per_step)
-    if w.launches_per_step == 1 and world == 1:
-        # one launch of the dominant kernel per step: its average duration is
-        # the back-to-back region's time per step (an upper bound: it also
-        # holds the gaps between launches)
+    if world == 1:
+        # the dominant kernel's average duration is at most the back-to-back
+        # region's time per step (which also holds the gaps between launches
+        # and, for the fp32 GEMM, its two tf32 split kernels)
         kernel_ms = ms_per_step
-        kernel_how = "timed region (CUDA events at its ends) / steps, one launch per step"
+        kernel_how = ("timed region (CUDA events at its ends) / steps"
+                      + ("" if w.launches_per_step == 1 else
+                         f" ({w.launches_per_step} launches per step, all counted)"))
     else:
         kernel_ms = per_call_ms
         kernel_how = "per-step CUDA events around each call" + (
