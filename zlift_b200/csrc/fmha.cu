@@ -32,6 +32,7 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cmath>
 #include <cstdlib>
@@ -65,6 +66,7 @@ struct FCfg {
 struct FParams {
     int heads, kv_ratio, sq, sk;
     int npairs, nkt;             // query-tile pairs, key tiles
+    int chunk;                   // (batch, head) pairs per scheduling chunk
     long long bh_begin, bh_count;
     long long ob, oh, orr;       // output strides (elements)
     void* o;
@@ -172,11 +174,16 @@ fmha_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-    // the query-tile pairs of one (batch, head) are consecutive blocks, so the
-    // CTAs resident at a time share that head's K and V in L2; within a head
-    // the heavy (late, causal) pairs go first
-    const int pair = p.npairs - 1 - (int)(blockIdx.x % p.npairs);
-    const long long bh = p.bh_begin + (long long)(blockIdx.x / p.npairs);
+    // Blocks go in chunks of p.chunk (batch, head) pairs whose K and V fit
+    // in L2 together; inside a chunk the query-tile pairs go heaviest first
+    // across all its heads (with a causal mask the late pairs have the most
+    // key tiles), so the last blocks to start are the shortest ones.
+    const long long per_chunk = (long long)p.chunk * p.npairs;
+    const long long ck = blockIdx.x / per_chunk;
+    const int in_chunk = (int)(blockIdx.x - ck * per_chunk);
+    const long long ck_heads = min((long long)p.chunk, p.bh_count - ck * p.chunk);
+    const int pair = p.npairs - 1 - (int)(in_chunk / ck_heads);
+    const long long bh = p.bh_begin + ck * p.chunk + in_chunk % ck_heads;
     const int b = (int)(bh / p.heads), h = (int)(bh % p.heads);
     const int hk = h / p.kv_ratio;
     // (scalars, not arrays: the warps index them by tile and an indexed array
@@ -586,6 +593,21 @@ int fmha_fwd(const AttnDesc& d, cudaStream_t s) {
                  (d.bb * 2) % 16 == 0;
     const long long grid = (long long)p.npairs * p.bh_count;
     if (grid > 0x7fffffffLL) return 1;
+    // scheduling chunks: the (batch, head) pairs whose K and V fit in 16 MB,
+    // rounded down to a power of two (8 heads of 4096 keys at head_dim 128).
+    // Measured on B200 with the causal 4096-key case over 256 and over 32
+    // heads: chunks of 8 ran 2.6 % and 20 % faster than head-by-head order;
+    // 8-32 were within 1 % of each other, chunks that split the heads
+    // unevenly (12, 24) or small ones (2, 4) slower.  ZBLAS_FMHA_CHUNK
+    // overrides (1 = head by head).
+    {
+        const long long kv = 2LL * d.sk * d.d * 2;
+        const long long fit = kv > 0 ? std::max(1LL, (16LL << 20) / kv) : 1;
+        long long ch = 1;
+        while (ch * 2 <= fit) ch *= 2;
+        if (const char* e = getenv("ZBLAS_FMHA_CHUNK")) ch = atoll(e);
+        p.chunk = (int)std::max(1LL, std::min(ch, p.bh_count));
+    }
     if (d.d == 128)
         return d.elem == 1 ? launch_bias<128, true>(tq, tk, tv, p, grid, s)
                            : launch_bias<128, false>(tq, tk, tv, p, grid, s);
