@@ -179,3 +179,43 @@ def test_fmha_bias_strided(oracle_lib, cuda):
     got = as_float(from_dev(do.reshape(-1), "bf16").reshape(q.shape), "bf16")
     assert normwise(got, as_float(o_ref, "bf16")) <= O_TOL
     assert np.max(np.abs(dl.cpu().numpy() - lse_ref)) <= LSE_TOL
+
+
+@pytest.mark.parametrize("chunk", ["1", "3", "5", "64"])
+def test_flash_block_order_chunks(oracle_lib, cuda, chunk, monkeypatch):
+    """The block -> (batch, head, query-tile pair) order in chunks of heads
+    (ZBLAS_FMHA_CHUNK; the default depends on the K/V size): every pair is
+    computed exactly once for chunk sizes that divide the 2 x 7 heads, leave
+    a partial last chunk, or exceed them; outputs start as NaN, so a pair
+    that was skipped or written twice with another's data fails."""
+    monkeypatch.setenv("ZBLAS_FMHA_CHUNK", chunk)
+    run_flash(oracle_lib, "bf16", 2, 640, 640, 7, 7, 128, True, seed=31)
+
+
+@pytest.mark.parametrize("chunk", ["2", "16"])
+def test_flash_pair_range_chunks(oracle_lib, cuda, chunk, monkeypatch):
+    """A (batch, head) sub-range (what one rank of a split runs) in chunks:
+    the pairs of the range are computed, the rest of O is left untouched."""
+    import torch
+    import zlift_b200
+    from zlift_b200 import attention, partition, blas
+    monkeypatch.setenv("ZBLAS_FMHA_CHUNK", chunk)
+    B, S, H, D = 2, 512, 5, 128
+    q, k, v = _qkv("bf16", B, S, S, H, H, D, 41)
+    o_ref, lse_ref = oracle_lib.attention(q, k, v, True, 1.0 / math.sqrt(D), 1)
+    dq, dk, dv = _dev4(q, "bf16"), _dev4(k, "bf16"), _dev4(v, "bf16")
+    do = torch.full_like(dq, float("nan"))
+    dl = torch.full((B, H, S), float("nan"), dtype=torch.float32, device=dq.device)
+    blk = attention.flash_block(dq, dk, dv, do, dl, causal=True)
+    lo, hi = 3, 9                      # (batch, head) pairs 3..8: b0 h3-4, b1 h0-3
+    assert partition.flash_pairs(blk, 1, lo, hi) == 0
+    torch.cuda.synchronize()
+    assert blas.device_error() == 0
+    o = as_float(from_dev(do.reshape(-1), "bf16").reshape(q.shape), "bf16")
+    want = as_float(o_ref, "bf16")
+    for pair in range(B * H):
+        b, h = divmod(pair, H)
+        if lo <= pair < hi:
+            assert normwise(o[b, :, h], want[b, :, h]) <= O_TOL
+        else:
+            assert np.all(np.isnan(o[b, :, h]))
