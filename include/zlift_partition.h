@@ -108,7 +108,10 @@ ZLIFT_API int zlift_part_gemm_ex_nsplit_overlap(
  * DONE, so its peers time out rather than read partial columns).  Up to 8
  * ranks.  Each exchange step waits at most 120 s for the other ranks, then
  * aborts the communicator (200).  0 success, 1 bad arguments, 13 a CUDA call
- * failed, 100 + ncclResult_t, 200 a rank did not arrive. */
+ * failed (on this rank or, reported through the agreement, on another);
+ * 100 + ncclResult_t (a collective failed) and 200 (a rank did not arrive)
+ * mean this rank's communicator has been aborted: it must not be used or
+ * destroyed afterwards. */
 ZLIFT_API int zlift_part_register_peer_buffer(void *comm, int nranks, int rank, void *C,
                                              size_t bytes);
 /* Unmaps a registered C (after every rank's last use of it; waits for the

@@ -507,12 +507,18 @@ int zlift_part_register_peer_buffer(void* comm, int nranks, int rank, void* C, s
     // Every rank takes part in both all-gathers, even one that failed above
     // (it sends zeros, then its error code), so no rank waits for it.  Each
     // gather is waited for with a deadline: a rank that never arrives aborts
-    // the communicator (200) instead of blocking here.
+    // the communicator (200) instead of blocking here.  A gather that cannot
+    // even be enqueued leaves the communicator in an unknown state and
+    // aborts it too, so a result >= 100 always means "aborted".
     bool aborted = false;
     auto gather = [&](const void* send, void* recv, size_t count) {
         NcclResult r = nc.all_gather(send, recv, count, kNcclInt8, comm, st);
         if (r != kNcclSuccess) {
-            if (rc == 0) rc = 100 + r;
+            nc.comm_abort(comm);
+            release_overlap(comm);
+            release_peer_bufs(comm);
+            aborted = true;
+            rc = 100 + r;
             return;
         }
         const int w = zlift_part_comm_wait(comm, st, kRegisterTimeoutMs);

@@ -104,10 +104,15 @@ class Comm:
 
     def register_peer_buffer(self, C, nbytes: int) -> int:
         """Collective: maps C into every rank (zlift_part_register_peer_buffer),
-        so the overlapped N-split gathers into it by peer stores."""
+        so the overlapped N-split gathers into it by peer stores.  A result of
+        100 or more means the library aborted the communicator (a collective
+        failed, or a rank did not arrive); this object then drops it."""
         from .blas import _ptr
-        return self.lib.zlift_part_register_peer_buffer(self.c, self.nranks, self.rank, _ptr(C),
-                                                        nbytes)
+        rc = self.lib.zlift_part_register_peer_buffer(self.c, self.nranks, self.rank, _ptr(C),
+                                                      nbytes)
+        if rc >= 100:
+            self.c = None
+        return rc
 
     def unregister_peer_buffer(self, C) -> int:
         from .blas import _ptr
