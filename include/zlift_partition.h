@@ -98,7 +98,9 @@ ZLIFT_API int zlift_part_gemm_ex_nsplit_overlap(
  * the communicator) and gives it a flag array.  Collective: every rank calls
  * it with its own C, the same `bytes`, before the first step that uses it;
  * the buffer ends up registered on every rank or on none (the ranks agree on
- * the first nonzero status).  Afterwards zlift_part_gemm_ex_nsplit_overlap on
+ * the first nonzero status).  A C already registered with this communicator
+ * returns 0 at once, without the exchange, so every rank must make the same
+ * calls in the same order.  Afterwards zlift_part_gemm_ex_nsplit_overlap on
  * this C gathers each sub-block straight into the peers' C instead of
  * through ncclAllGather: by copy-engine copies, one stream per peer
  * (default), or by a store kernel next to the GEMM of the following
